@@ -1,0 +1,415 @@
+#!/usr/bin/env python
+"""bench.py — NVFP4 GEMM throughput on B200, one process per GPU.
+
+Headline: TFLOP/s of the block-scaled NVFP4 GEMM on the square workload M = N = K = 8192
+(A, B bf16 N(0,1), seed 2, quantized on the GPU with the reference recipe), at 1..8 GPUs.
+N > 1 is column-parallel (weak scaling): every rank owns an 8192-column shard of a global
+M x (8192*P) x K product (its own slice of B and B's scale factors, A replicated), with no
+data-path collective; `value` is the work of all ranks over the max-over-ranks device time.
+
+One JSON line on rank 0. Besides the contract keys it carries:
+  roofline      the GEMM kernel against the FP4 dense peak (4 x the measured cuBLAS bf16 rate)
+  cpu_baseline  the CPU oracle port (dequantize + fp32 matmul) on a bounded row sample
+  e2e           the same metric through my_plugins.gemm_nvfp4 with pinned host buffers,
+                host->device copies of the operands and device->host copy of D in the timing
+  quantize / dequantize   GB/s of the 8192x8192 activation workload (0.5% x50 outliers)
+  clocks        SM clock samples (nvidia-smi) from warm-up start to the end of timing
+
+`--impl reference` times the CPU implementation of the reference arithmetic (the oracle port;
+the reference ships no CPU code and its GEMM does not build for sm_100a) on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M_SQ = N_SQ = K_SQ = 8192
+L2_FLUSH_BYTES = 256 << 20          # > 126 MB L2
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+NOMINAL_FP4_TFLOPS = 9000.0
+QUANT_BYTES = 8192 * 8192 * 2 + 8192 * 4096 + 8192 * 512   # 171,966,464 per pass
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-quant", action="store_true")
+    ap.add_argument("--size", type=int, default=8192, help="M = N = K (profiling of small cases)")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def profiled_traffic(key):
+    """DRAM bytes per launch from a committed ncu summary (profiles/traffic.json), else None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(key)
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi samples of one GPU while it runs (started before warm-up, stopped after)."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.12)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in (getattr(self, "out", "") or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or (self.uuid and f[0] != self.uuid):
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), float(f[3]), f[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        max_mhz = max(r[1] for r in rows)
+        loaded = [r for r in rows if r[2] > 200.0] or rows  # samples under load (power > 200 W)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max_mhz,
+                "reasons": reasons, "samples": len(loaded),
+                "power_w_max": max(r[2] for r in rows)}
+
+
+def gpu_uuid(torch, dev):
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------------------------------------
+def dist_setup(torch):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(torch, world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(torch, world, value):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_square_operands(torch, plugins, size, rank):
+    """A (replicated, seed 2) and this rank's B shard (seed 2 + rank) quantized on the GPU."""
+    g = torch.Generator(device="cuda").manual_seed(2)
+    A = torch.randn(size, size, device="cuda", generator=g).to(torch.bfloat16)
+    if rank > 0:
+        g = torch.Generator(device="cuda").manual_seed(2 + rank)
+    B = torch.randn(size, size, device="cuda", generator=g).to(torch.bfloat16)
+    sA = 6 * 448 / A.abs().max().to(dtype=torch.float32)
+    sB = 6 * 448 / B.abs().max().to(dtype=torch.float32)
+    a, a_sf = plugins.quantize_nvfp4(A, sA)
+    b, b_sf = plugins.quantize_nvfp4(B, sB)
+    del A, B
+    return a, b, a_sf, b_sf, (sA * sB).reshape(())
+
+
+def time_device(torch, fn, steps, warmup, flush, world):
+    """Warm-up, then `steps` launches each timed by CUDA events on the current stream, with an
+    L2 flush (untimed) before each. Returns the summed device milliseconds (max over ranks)."""
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        fn()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    barrier(torch, world)
+    for s, e in ev:
+        flush.zero_()
+        s.record(stream)
+        fn()
+        e.record(stream)
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    total = sum(s.elapsed_time(e) for s, e in ev)
+    return max_over_ranks(torch, world, total)
+
+
+def cpu_baseline_gemm(a, b, a_sf, b_sf, scale, rows=256, budget_s=10.0):
+    """Oracle port of the reference arithmetic on the host: decode the block-scaled operands,
+    fp32 matmul (torch, all host threads), / scale, bf16. Bounded sample: `rows` rows of A."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    A = a[:rows].cpu().numpy()
+    Asf = a_sf[:rows].view(torch.uint8).cpu().numpy()
+    B = b.cpu().numpy()
+    Bsf = b_sf.view(torch.uint8).cpu().numpy()
+    s = np.float32(scale.item())
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while True:
+        t0 = time.perf_counter()
+        fa = torch.from_numpy(O.decode_scaled(A, Asf))
+        fb = torch.from_numpy(O.decode_scaled(B, Bsf))
+        d = (fa @ fb.T) / torch.tensor(s)
+        d = d.to(torch.bfloat16)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(times) >= 5:
+            break
+    t = statistics.median(times)
+    flops = 2.0 * rows * B.shape[0] * A.shape[1] * 2
+    return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{rows} of {a.shape[0]} rows of A x full B ({B.shape[0]}x{A.shape[1]*2}); "
+                      f"median of {len(times)} runs; oracle decode (OpenMP, {O.num_threads()} "
+                      f"threads) + torch fp32 matmul; os.cpu_count()={os.cpu_count()}"}
+
+
+def run_reference_arm(args):
+    """CPU implementation of the reference arithmetic on the same workload (rank 0 only)."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    size = args.size
+    rows = 128
+    rng = np.random.default_rng(2)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import nvfp4_cases as cases
+    Ab = cases.activation(rng, rows, size)
+    Bb = cases.activation(rng, size, size)
+    sA, sB = O.global_scale(Ab), O.global_scale(Bb)
+
+    def step():
+        qa, fa = O.quantize(Ab, sA)        # activation quantize (the sample's rows)
+        qb, fb = O.quantize(Bb, sB)
+        da = torch.from_numpy(O.decode_scaled(qa, fa))
+        db = torch.from_numpy(O.decode_scaled(qb, fb))
+        d = ((da @ db.T) / torch.tensor(np.float32(sA) * np.float32(sB))).to(torch.bfloat16)
+        return d
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    flops = 2.0 * rows * size * size
+    val = flops / dt / 1e12
+    cores = torch.get_num_threads()
+    sample = (f"{rows} of {size} rows of A x full B ({size}x{size}), per step: quantize A-rows and "
+              f"B (oracle, OpenMP {O.num_threads()} threads) + decode + torch fp32 matmul + bf16")
+    line = {"metric": "nvfp4_gemm_tflops", "value": val, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/ue4m3->f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"square_gemm_{size}", "M": size, "N": size, "K": size},
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    from my_nvfp4_gemm_b200 import capi, load_my_plugins
+    plugins = load_my_plugins()
+    world, rank, local = dist_setup(torch)
+    dev = torch.cuda.current_device()
+    size = args.size
+    M = N = K = size
+    flops = 2.0 * M * N * K
+    hbm_gbs, bf16_tf, peak_src = measured_peaks()
+    fp4_peak = 4.0 * bf16_tf
+
+    a, b, a_sf, b_sf, scale = make_square_operands(torch, plugins, size, rank)
+    d = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    stream_h = torch.cuda.current_stream().cuda_stream
+    ptrs = (a.data_ptr(), b.data_ptr(), a_sf.data_ptr(), b_sf.data_ptr(), scale.data_ptr(), d.data_ptr())
+
+    def gemm_once():
+        st = capi.gemm(*ptrs, M, N, K, stream_h)
+        if st:
+            raise capi.NvFp4Error(st, "nvfp4_gemm")
+
+    sampler = ClockSampler(gpu_uuid(torch, dev))
+    with sampler:
+        gemm_ms_total = time_device(torch, gemm_once, args.steps, args.warmup, flush, world)
+    clocks = sampler.summary()
+    ms = gemm_ms_total / args.steps
+    value = world * flops / (ms * 1e-3) / 1e12
+    achieved = flops / (ms * 1e-3) / 1e12
+    traffic = profiled_traffic(f"gemm_square_{size}")
+
+    line = {
+        "metric": "nvfp4_gemm_tflops", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/ue4m3->f32",
+        "data": "synthetic",
+        "config": {"workload": f"square_gemm_{size}", "M": M, "N": N * world, "K": K,
+                   "n_per_rank": N, "parallelism": f"column-parallel N x{world}",
+                   "l2": "flushed (256 MiB write) before every timed launch",
+                   "inputs": "bf16 N(0,1) seed 2 (B shard seed 2+rank), quantized on device"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp4_peak,
+                     "unit": "TFLOP/s", "frac": achieved / fp4_peak, "traffic": traffic,
+                     "peak_source": f"4 x {peak_src} cuBLAS bf16 burst ({bf16_tf:.1f} TF/s)",
+                     "frac_of_nominal_9000": achieved / NOMINAL_FP4_TFLOPS,
+                     "kernel": "nvfp4::gemm::gemm_kernel (tcgen05 mxf4nvf4)"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+
+    # ---- quantize / dequantize (8192x8192 activation with 0.5% x50 outliers, seed 1)
+    if not args.no_quant and size == 8192:
+        g = torch.Generator(device="cuda").manual_seed(1)
+        X = torch.randn(8192, 8192, device="cuda", generator=g)
+        idx = torch.randperm(X.numel(), device="cuda", generator=g)[: int(0.005 * X.numel())]
+        X.view(-1)[idx] *= 50.0
+        X = X.to(torch.bfloat16)
+        sX = (6 * 448 / X.abs().max().to(torch.float32)).reshape(())
+        q = torch.empty(8192, 4096, dtype=torch.uint8, device="cuda")
+        qsf = torch.empty(8192, 512, dtype=torch.uint8, device="cuda")
+        y = torch.empty_like(X)
+
+        def quant_once():
+            capi.check(capi.quantize(X.data_ptr(), sX.data_ptr(), X.numel(), q.data_ptr(),
+                                     qsf.data_ptr(), stream_h), "nvfp4_quantize")
+
+        def dequant_once():
+            capi.check(capi.dequantize(q.data_ptr(), sX.data_ptr(), qsf.data_ptr(), q.numel(),
+                                       y.data_ptr(), stream_h), "nvfp4_dequantize")
+
+        for name, fn in (("quantize", quant_once), ("dequantize", dequant_once)):
+            t = time_device(torch, fn, args.steps, args.warmup, flush, world) / args.steps
+            gbs = QUANT_BYTES / (t * 1e-3) / 1e9
+            line[name] = {"value": world * gbs, "unit": "GB/s", "ms_per_call": t,
+                          "workload": "8192x8192 bf16, 0.5% x50 outliers, seed 1",
+                          "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_gbs,
+                                       "unit": "GB/s", "frac": gbs / hbm_gbs,
+                                       "traffic": profiled_traffic(f"{name}_8192"),
+                                       "peak_source": f"{peak_src} copy bandwidth"}}
+            line["gpu_launches"] += args.steps
+        del X, y, q, qsf
+
+    # ---- end to end through the torch module with pinned host buffers
+    if not args.no_e2e:
+        ha = a.cpu().pin_memory()
+        hb = b.cpu().pin_memory()
+        hasf = a_sf.cpu().pin_memory()
+        hbsf = b_sf.cpu().pin_memory()
+        hd = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+        da, db = torch.empty_like(a), torch.empty_like(b)
+        dasf, dbsf = torch.empty_like(a_sf), torch.empty_like(b_sf)
+        scale_h = scale.cpu()
+
+        def e2e_once():
+            da.copy_(ha, non_blocking=True)
+            db.copy_(hb, non_blocking=True)
+            dasf.copy_(hasf, non_blocking=True)
+            dbsf.copy_(hbsf, non_blocking=True)
+            out = plugins.gemm_nvfp4(da, db, dasf, dbsf, scale_h)
+            hd.copy_(out, non_blocking=True)
+
+        e2e_steps = max(3, min(args.steps, 20))
+        t = time_device(torch, e2e_once, e2e_steps, 2, flush, world) / e2e_steps
+        h2d = sum(t_.numel() * t_.element_size() for t_ in (ha, hb, hasf, hbsf))
+        line["e2e"] = {"value": world * flops / (t * 1e-3) / 1e12, "unit": "TFLOP/s",
+                       "ms_per_step": t, "steps": e2e_steps, "h2d_bytes_per_step": h2d,
+                       "d2h_bytes_per_step": hd.numel() * 2,
+                       "api": "my_plugins.gemm_nvfp4, pinned host operands in, bf16 D out"}
+        line["gpu_launches"] += e2e_steps
+
+    # ---- CPU baseline (rank 0, N = 1 only)
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_gemm(a, b, a_sf, b_sf, scale)
+
+    st = capi.device_status(stream_h)
+    if st != 0:
+        line["device_status"] = capi.STATUS_NAMES.get(st, st)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

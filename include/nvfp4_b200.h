@@ -1,0 +1,124 @@
+/*
+ * nvfp4_b200.h — C ABI of the B200 (sm_100a) NVFP4 quantize / dequantize / GEMM library.
+ *
+ * Packed format (unchanged from the reference plugin):
+ *   - two E2M1 codes per byte, the element with the even index in the low nibble;
+ *   - one UE4M3 scale factor per 16 consecutive elements along the last (K) dimension,
+ *     stored row-major as [rows, K/16];
+ *   - one fp32 per-tensor scale `s = 6*448/amax` (the reciprocal of the usual
+ *     "global scale"), exactly as the reference's test recipe builds it.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, 64-bit sizes and a cudaStream_t; the caller owns all buffers;
+ *   - is asynchronous on `stream` and allocates nothing;
+ *   - returns NVFP4_OK or an nvfp4_status_t error code and never exits the process;
+ *   - must be called with the device that owns the buffers current (like cuBLAS).
+ *
+ * Scales come in two forms, mirroring the reference's by-value float while removing its
+ * per-call device->host synchronisation:
+ *   - `const float* scale`  : a device pointer to one fp32 value (read by the kernel);
+ *   - `*_host_scale` variant : the fp32 value itself, as the reference launchers take it.
+ */
+#ifndef NVFP4_B200_H_
+#define NVFP4_B200_H_
+
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum nvfp4_status_t {
+  NVFP4_OK = 0,
+  NVFP4_ERR_INVALID_VALUE = 1,     /* null pointer, negative size, bad argument */
+  NVFP4_ERR_UNSUPPORTED_SHAPE = 2, /* e.g. K % 256 != 0, N % 8 != 0, numel % 16 != 0 */
+  NVFP4_ERR_MISALIGNED = 3,        /* a pointer lacks the alignment its kernel needs */
+  NVFP4_ERR_CUDA = 4,              /* a CUDA runtime call or kernel launch failed */
+  NVFP4_ERR_NO_DEVICE = 5,         /* no sm_100 device current, or driver entry point missing */
+  NVFP4_ERR_DEVICE_TIMEOUT = 6,    /* a bounded device-side wait gave up (see nvfp4_device_status) */
+  NVFP4_ERR_TOO_LARGE = 7          /* a size exceeds what the kernel addresses */
+} nvfp4_status_t;
+
+/* Human-readable name of a status code (static storage, never NULL). */
+const char* nvfp4_status_string(int status);
+
+/* Library version, e.g. 0x000100 for 0.1.0. */
+int nvfp4_version(void);
+
+/*
+ * Quantize bf16 -> NVFP4 (packed E2M1 + UE4M3 per 16 elements).
+ * Replaces my_plugins::quantize_nvfp4 (csrc/quantize/quantize_nvfp4.h:6, launcher
+ * csrc/quantize/quantize_nvfp4.cu:37-41). The reference passes the bf162 pair count as
+ * `int`; here `numel` is the number of bf16 elements (= 2 x the reference's count), int64.
+ *   input      : bf16[numel], 16-byte aligned, treated as a flat array of 16-element blocks
+ *   input_scale: device pointer to fp32 s (= 6*448/amax)
+ *   output     : uint8[numel/2], 4-byte aligned
+ *   output_sf  : e4m3[numel/16]
+ * Requires numel % 16 == 0. numel == 0 is a no-op.
+ */
+int nvfp4_quantize(const void* input, const float* input_scale, int64_t numel,
+                   void* output, void* output_sf, cudaStream_t stream);
+/* Same, with the scale passed by value (the reference launcher's form). */
+int nvfp4_quantize_host_scale(const void* input, float input_scale, int64_t numel,
+                              void* output, void* output_sf, cudaStream_t stream);
+
+/*
+ * Dequantize NVFP4 -> bf16.
+ * Replaces my_plugins::de_quantize_nvfp4 (csrc/quantize/quantize_nvfp4.h:7, launcher
+ * csrc/quantize/quantize_nvfp4.cu:64-68). `n_bytes` is the packed byte count, as in the
+ * reference (input.numel() of the uint8 tensor), widened to int64.
+ *   input      : uint8[n_bytes], 4-byte aligned
+ *   input_scale: device pointer to fp32 s
+ *   input_sf   : e4m3[n_bytes/8]
+ *   output     : bf16[2*n_bytes], 16-byte aligned
+ * Requires n_bytes % 8 == 0.
+ */
+int nvfp4_dequantize(const void* input, const float* input_scale, const void* input_sf,
+                     int64_t n_bytes, void* output, cudaStream_t stream);
+int nvfp4_dequantize_host_scale(const void* input, float input_scale, const void* input_sf,
+                                int64_t n_bytes, void* output, cudaStream_t stream);
+
+/*
+ * Block-scaled NVFP4 GEMM, "TN": D[m,n] = bf16( sum_k a[m,k]*sfa[m,k/16]*b[n,k]*sfb[n,k/16] / scale ).
+ * Replaces my_plugins::gemm_nvfp4 (csrc/gemm/gemm_nvfp4.h:44-47, launcher
+ * csrc/gemm/gemm_nvfp4.cu:242-252). Sizes are int64 instead of int; failures return a status
+ * instead of assert()/exit().
+ *   A    : uint8[M, K/2]  packed E2M1, K-major
+ *   B    : uint8[N, K/2]  packed E2M1, K-major
+ *   A_sf : e4m3[M, K/16]  row-major
+ *   B_sf : e4m3[N, K/16]  row-major
+ *   scale: device pointer to fp32 (the product s_A*s_B of the two tensors' scales)
+ *   D    : bf16[M, N] row-major
+ * Requires K % 256 == 0 and N % 8 == 0 (the reference's preconditions); any M >= 0.
+ * All pointers must be 16-byte aligned (TMA).
+ */
+int nvfp4_gemm(const void* A, const void* B, const void* A_sf, const void* B_sf,
+               const float* scale, void* D, int64_t M, int64_t N, int64_t K,
+               cudaStream_t stream);
+int nvfp4_gemm_host_scale(const void* A, const void* B, const void* A_sf, const void* B_sf,
+                          float scale, void* D, int64_t M, int64_t N, int64_t K,
+                          cudaStream_t stream);
+
+/*
+ * Device-side status word, shared by all kernels of this library on the current device.
+ * Kernels that wait on barriers give up after a bounded time, record
+ * NVFP4_ERR_DEVICE_TIMEOUT here and return instead of hanging. Reading synchronises `stream`.
+ * The reference has no counterpart (its waits spin forever, csrc/common/common.h:158-170).
+ */
+int nvfp4_device_status(int* status_out, cudaStream_t stream);
+int nvfp4_clear_device_status(cudaStream_t stream);
+
+/*
+ * Self-test of the bounded-wait path: launches one warp that waits on a barrier nothing
+ * ever completes, with the given limit in nanoseconds. The wait gives up, records
+ * NVFP4_ERR_DEVICE_TIMEOUT in the device status word and the kernel returns normally.
+ * No reference counterpart.
+ */
+int nvfp4_selftest_wait_timeout(uint64_t timeout_ns, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVFP4_B200_H_ */

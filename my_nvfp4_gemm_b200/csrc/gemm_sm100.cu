@@ -1,0 +1,547 @@
+// gemm_sm100.cu — block-scaled NVFP4 GEMM for B200 (sm_100a) on the 5th-generation tensor cores.
+//
+//   D[m, n] = bf16( sum_k e2m1(A[m,k]) sfA[m,k/16] e2m1(B[n,k]) sfB[n,k/16] / scale )
+//
+// Same operands, layouts and result as the reference kernel (csrc/gemm/gemm_nvfp4.cu:5-240):
+// A [M, K/2] and B [N, K/2] packed E2M1, both K-major ("TN"); row-major UE4M3 scale factors
+// [rows, K/16]; fp32 accumulation; bf16 row-major output. The reference's SM120 warp-level
+// mma.sync design does not exist on sm_100a and is not followed. This kernel is:
+//
+//   * persistent: one CTA per SM walks output tiles of 128 x BN (BN = 256 or 128);
+//   * warp-specialised (256 threads):
+//       warp 0  TMA producer: A/B tiles (128B-swizzled) and scale-factor tiles into a
+//               STAGES-deep shared-memory ring, guarded by full and empty mbarriers;
+//       warp 1  MMA issuer: owns the tensor-memory allocation, copies the stage's scale factors
+//               into TMEM (tcgen05.cp) and issues tcgen05.mma .kind::mxf4nvf4
+//               .block_scale.scale_vec::4X (M=128, N=BN, K=64) into a TMEM fp32 accumulator;
+//       warp 2  scale-factor transposer: the API's row-major scale factors are rearranged in
+//               shared memory into the 32-lane x 4-column chunks the MMA reads from TMEM;
+//       warps 4-7 epilogue: tcgen05.ld of the accumulator, x (1/scale), bf16 convert, staged
+//               through 64B-swizzled shared memory and written with TMA tensor stores
+//               (bounds-clipped, so ragged M and N need no masking);
+//   * fault-safe: every mbarrier wait is bounded; a wait that times out raises a CTA-wide abort
+//     flag, every role returns, copies and MMAs in flight are drained (bounded), TMEM is freed,
+//     and NVFP4_ERR_DEVICE_TIMEOUT is recorded in the device status word.
+// No TMA load uses cluster multicast.
+#include <cstdint>
+#include <mutex>
+
+#include "capi_util.h"
+#include "ptx.cuh"
+
+// Device status word (NVFP4_OK or the first error a kernel recorded).
+__device__ int g_nvfp4_device_status = 0;
+
+namespace nvfp4 {
+namespace gemm {
+
+constexpr int kBM = 128;            // MMA M (one CTA, tcgen05 cta_group::1)
+constexpr int kBK = 256;            // K elements per pipeline stage = 128 packed bytes
+constexpr int kBKBytes = kBK / 2;
+constexpr int kUmmaK = 64;          // K per tcgen05.mma kind::mxf4nvf4
+constexpr int kKSteps = kBK / kUmmaK;
+constexpr int kSfBytesPerRow = kBK / 16;  // 16 scale bytes per row per stage
+constexpr int kThreads = 256;
+constexpr int kNumEpiWarps = 4;
+constexpr int kEpiCols = 32;              // accumulator columns per epilogue store
+constexpr int kEpiBufBytes = 32 * kEpiCols * 2;  // 32 rows x 32 bf16 per epilogue warp
+
+template <int BN_, int STAGES_, int ACC_STAGES_>
+struct Cfg {
+  static constexpr int BN = BN_;
+  static constexpr int STAGES = STAGES_;
+  static constexpr int ACC_STAGES = ACC_STAGES_;
+  static_assert(BN % 128 == 0 && BN <= 256, "BN must be 128 or 256");
+
+  static constexpr int A_STAGE = kBM * kBKBytes;           // 16 KiB
+  static constexpr int B_STAGE = BN * kBKBytes;
+  static constexpr int SFA_STAGE = kBM * kSfBytesPerRow;   // 2 KiB
+  static constexpr int SFB_STAGE = BN * kSfBytesPerRow;
+  static constexpr uint32_t STAGE_TX = A_STAGE + B_STAGE + SFA_STAGE + SFB_STAGE;
+
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
+  static constexpr int OFF_SFA = OFF_B + STAGES * B_STAGE;
+  static constexpr int OFF_SFB = OFF_SFA + STAGES * SFA_STAGE;
+  static constexpr int OFF_EPI = OFF_SFB + STAGES * SFB_STAGE;
+  static constexpr int OFF_BAR = OFF_EPI + kNumEpiWarps * kEpiBufBytes;
+  static constexpr int NUM_BARS = 3 * STAGES + 2 * ACC_STAGES + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16;
+  static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;     // slack to align the base to 1 KiB
+  static_assert(SMEM_ALLOC <= 232448, "shared memory budget exceeded");
+
+  // Tensor memory columns: accumulators, then per-K-step scale-factor chunks.
+  static constexpr uint32_t SFA_COLS_PER_STEP = 4;          // 128 rows -> one 32x4 chunk
+  static constexpr uint32_t SFB_COLS_PER_STEP = BN / 32;    // BN/128 chunks of 4 columns
+  static constexpr uint32_t COL_SFA = BN * ACC_STAGES;
+  static constexpr uint32_t COL_SFB = COL_SFA + kKSteps * SFA_COLS_PER_STEP;
+  static constexpr uint32_t COLS_USED = COL_SFB + kKSteps * SFB_COLS_PER_STEP;
+  static constexpr uint32_t TMEM_COLS = COLS_USED <= 32 ? 32 : COLS_USED <= 64 ? 64
+                                      : COLS_USED <= 128 ? 128 : COLS_USED <= 256 ? 256 : 512;
+  static_assert(COLS_USED <= 512, "tensor memory budget exceeded");
+};
+
+struct Params {
+  const float* scale_ptr;  // device scalar, or nullptr -> scale_val
+  float scale_val;
+  int m;                   // rows of D
+  int n;                   // columns of D
+  int m_blocks;
+  int n_blocks;
+  int k_stages;
+  uint64_t timeout_ns;
+};
+
+// In-place rearrangement of one 128-row scale-factor chunk held row-major (row r at r*16 bytes,
+// 4-byte word j = the 4 scale factors of K-step j) into four 512-byte chunks, one per K-step j,
+// each laid out as 32 rows x 16 bytes where row r holds step j's word of rows r, r+32, r+64,
+// r+96. tcgen05.cp .32x128b.warpx4 copies such a chunk into TMEM (lane r, columns c..c+3) and
+// replicates it into the four lane quarters, which is where the block-scaled MMA reads the
+// scale factor of row 32*q + r (column c + q). Executed by one full warp; conflict-free.
+__device__ __forceinline__ void transpose_sf_chunk(uint32_t base, int lane) {
+  uint4 w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) w[q] = ptx::ld_shared_v4(base + (32 * q + lane) * 16);
+  __syncwarp();
+  ptx::st_shared_v4(base + 0 * 512 + lane * 16, make_uint4(w[0].x, w[1].x, w[2].x, w[3].x));
+  ptx::st_shared_v4(base + 1 * 512 + lane * 16, make_uint4(w[0].y, w[1].y, w[2].y, w[3].y));
+  ptx::st_shared_v4(base + 2 * 512 + lane * 16, make_uint4(w[0].z, w[1].z, w[2].z, w[3].z));
+  ptx::st_shared_v4(base + 3 * 512 + lane * 16, make_uint4(w[0].w, w[1].w, w[2].w, w[3].w));
+}
+
+template <class C>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+            const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
+            const __grid_constant__ CUtensorMap tm_d, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sA = smem + C::OFF_A;
+  uint8_t* sB = smem + C::OFF_B;
+  uint8_t* sSFA = smem + C::OFF_SFA;
+  uint8_t* sSFB = smem + C::OFF_SFB;
+  uint8_t* sEPI = smem + C::OFF_EPI;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full_bar = bars;                                  // TMA -> transposer
+  uint64_t* sf_bar = bars + C::STAGES;                        // transposer -> MMA
+  uint64_t* empty_bar = bars + 2 * C::STAGES;                 // MMA (commit) -> TMA
+  uint64_t* tfull_bar = bars + 3 * C::STAGES;                 // MMA (commit) -> epilogue
+  uint64_t* tempty_bar = tfull_bar + C::ACC_STAGES;           // epilogue -> MMA
+  uint64_t* drain_bar = tempty_bar + C::ACC_STAGES;           // MMA drain before TMEM free
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.m_blocks * p.n_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::STAGES; ++i) {
+      ptx::mbar_init(&full_bar[i], 1);
+      ptx::mbar_init(&sf_bar[i], 1);
+      ptx::mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < C::ACC_STAGES; ++i) {
+      ptx::mbar_init(&tfull_bar[i], 1);
+      ptx::mbar_init(&tempty_bar[i], kNumEpiWarps);
+    }
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::tma_prefetch_desc(&tm_a);
+    ptx::tma_prefetch_desc(&tm_b);
+    ptx::tma_prefetch_desc(&tm_sfa);
+    ptx::tma_prefetch_desc(&tm_sfb);
+    ptx::tma_prefetch_desc(&tm_d);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    ptx::tmem_relinquish_alloc_permit();
+  }
+  ptx::tc_fence_before_sync();
+  __syncthreads();
+  ptx::tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t fills = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile % p.m_blocks) * kBM;
+        const int n0 = (tile / p.m_blocks) * C::BN;
+        for (int kb = 0; kb < p.k_stages; ++kb) {
+          if (!ptx::mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.timeout_ns)) goto producer_done;
+          ptx::mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_TX);
+          ptx::tma_load_2d(sA + stage * C::A_STAGE, &tm_a, &full_bar[stage], kb * kBKBytes, m0);
+          ptx::tma_load_2d(sB + stage * C::B_STAGE, &tm_b, &full_bar[stage], kb * kBKBytes, n0);
+          ptx::tma_load_2d(sSFA + stage * C::SFA_STAGE, &tm_sfa, &full_bar[stage], kb * kSfBytesPerRow, m0);
+          ptx::tma_load_2d(sSFB + stage * C::SFB_STAGE, &tm_sfb, &full_bar[stage], kb * kSfBytesPerRow, n0);
+          ++fills;
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    producer_done:
+      // Never leave a TMA write in flight into shared memory of an exiting CTA: wait (bounded,
+      // ignoring the abort flag) until the most recent fill of every slot has landed.
+      {
+        int no_abort = 0;
+        const int64_t last = fills < C::STAGES ? fills : C::STAGES;
+        for (int64_t i = 0; i < last; ++i) {
+          const int64_t f = fills - 1 - i;
+          ptx::mbar_wait(&full_bar[f % C::STAGES], uint32_t((f / C::STAGES) & 1), &no_abort,
+                         p.timeout_ns);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::make_idesc_mxf4nvf4(kBM, C::BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        if (!ptx::mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.timeout_ns)) goto mma_done;
+        ptx::tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * C::BN);
+        for (int kb = 0; kb < p.k_stages; ++kb) {
+          if (!ptx::mbar_wait(&sf_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
+          if (!ptx::mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
+          ptx::tc_fence_after_sync();
+          const uint32_t sfa_s = ptx::smem_u32(sSFA + stage * C::SFA_STAGE);
+          const uint32_t sfb_s = ptx::smem_u32(sSFB + stage * C::SFB_STAGE);
+#pragma unroll
+          for (int j = 0; j < kKSteps; ++j)
+            ptx::tc_cp_32x128b_warpx4(tmem_base + C::COL_SFA + j * C::SFA_COLS_PER_STEP,
+                                      ptx::make_smem_desc(sfa_s + j * 512, 0, 128, ptx::kLayoutNone));
+#pragma unroll
+          for (int c = 0; c < C::BN / 128; ++c)
+#pragma unroll
+            for (int j = 0; j < kKSteps; ++j)
+              ptx::tc_cp_32x128b_warpx4(
+                  tmem_base + C::COL_SFB + j * C::SFB_COLS_PER_STEP + 4 * c,
+                  ptx::make_smem_desc(sfb_s + c * 2048 + j * 512, 0, 128, ptx::kLayoutNone));
+          const uint32_t a_s = ptx::smem_u32(sA + stage * C::A_STAGE);
+          const uint32_t b_s = ptx::smem_u32(sB + stage * C::B_STAGE);
+#pragma unroll
+          for (int j = 0; j < kKSteps; ++j) {
+            // K-step j starts 32 bytes further along the 128-byte swizzled rows.
+            const uint64_t a_desc = ptx::make_smem_desc(a_s + j * 32, 0, 1024, ptx::kLayoutSW128);
+            const uint64_t b_desc = ptx::make_smem_desc(b_s + j * 32, 0, 1024, ptx::kLayoutSW128);
+            ptx::tc_mma_mxf4nvf4(d_tmem, a_desc, b_desc, idesc,
+                                 tmem_base + C::COL_SFA + j * C::SFA_COLS_PER_STEP,
+                                 tmem_base + C::COL_SFB + j * C::SFB_COLS_PER_STEP,
+                                 (kb | j) != 0 ? 1u : 0u);
+          }
+          ptx::tc_commit(&empty_bar[stage]);  // frees the smem slot once these MMAs are done
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+        ptx::tc_commit(&tfull_bar[acc]);      // accumulator ready for the epilogue
+        if (++acc == C::ACC_STAGES) { acc = 0; acc_phase ^= 1; }
+      }
+    mma_done:
+      // Drain every tcgen05 operation this thread issued before TMEM is released.
+      {
+        int no_abort = 0;
+        ptx::tc_commit(drain_bar);
+        ptx::mbar_wait(drain_bar, 0, &no_abort, p.timeout_ns);
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ scale-factor transposer
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int kb = 0; kb < p.k_stages; ++kb) {
+        const bool ok = ptx::mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns);
+        if (!__all_sync(0xFFFFFFFFu, ok)) goto transposer_done;
+        transpose_sf_chunk(ptx::smem_u32(sSFA + stage * C::SFA_STAGE), lane);
+#pragma unroll
+        for (int c = 0; c < C::BN / 128; ++c)
+          transpose_sf_chunk(ptx::smem_u32(sSFB + stage * C::SFB_STAGE + c * 2048), lane);
+        ptx::fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.cp
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&sf_bar[stage]);
+        if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  transposer_done:;
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int ew = warp - 4;  // == warp % 4: this warp may access TMEM lanes 32*ew .. 32*ew+31
+    const float scale = p.scale_ptr ? __ldg(p.scale_ptr) : p.scale_val;
+    const float alpha = __frcp_rn(scale);
+    uint8_t* buf = sEPI + ew * kEpiBufBytes;
+    const uint32_t buf_s = ptx::smem_u32(buf);
+    const uint32_t swz = uint32_t((lane >> 1) & 3);  // 64-byte TMA swizzle of row `lane`
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m0 = (tile % p.m_blocks) * kBM;
+      const int n0 = (tile / p.m_blocks) * C::BN;
+      const bool ok = ptx::mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.timeout_ns);
+      if (!__all_sync(0xFFFFFFFFu, ok)) break;
+      ptx::tc_fence_after_sync();
+      const uint32_t t_row = tmem_base + (uint32_t(ew * 32) << 16) + uint32_t(acc * C::BN);
+#pragma unroll 1
+      for (int c = 0; c < C::BN / kEpiCols; ++c) {
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(t_row + c * kEpiCols, r);
+        ptx::tmem_wait_ld();
+        if (c == C::BN / kEpiCols - 1) {
+          // The whole accumulator is in registers: hand TMEM back to the MMA warp.
+          ptx::tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+        }
+        uint32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          o[i] = ptx::f32x2_to_bf16x2(__uint_as_float(r[2 * i]) * alpha,
+                                      __uint_as_float(r[2 * i + 1]) * alpha);
+        if (lane == 0) ptx::bulk_wait_group_read<0>();  // previous store has read the buffer
+        __syncwarp();
+        const uint32_t row = buf_s + uint32_t(lane) * 64;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ptx::st_shared_v4(row + ((uint32_t(k) ^ swz) << 4),
+                            make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]));
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        // Boxes that start inside D are clipped by the TMA unit; boxes entirely outside
+        // (ragged M or N) are skipped.
+        if (lane == 0 && m0 + ew * 32 < p.m && n0 + c * kEpiCols < p.n) {
+          ptx::tma_store_2d(&tm_d, buf, n0 + c * kEpiCols, m0 + ew * 32);
+          ptx::bulk_commit_group();
+        }
+      }
+      if (++acc == C::ACC_STAGES) { acc = 0; acc_phase ^= 1; }
+    }
+    if (lane == 0) ptx::bulk_wait_group<0>();
+  }
+
+  ptx::tc_fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicCAS(&g_nvfp4_device_status, 0, NVFP4_ERR_DEVICE_TIMEOUT);
+  if (warp == 1) {
+    __syncwarp();
+    ptx::tc_fence_after_sync();
+    ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// K == 0: the sum is empty; D = bf16(0 / scale), as the reference epilogue would produce.
+__global__ void fill_empty_k_kernel(uint16_t* __restrict__ d, int64_t n, const float* scale_ptr,
+                                    float scale_val) {
+  const float scale = scale_ptr ? __ldg(scale_ptr) : scale_val;
+  const uint32_t v = ptx::f32x2_to_bf16x2(__fdiv_rn(0.0f, scale), 0.0f) & 0xFFFFu;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x)
+    d[i] = static_cast<uint16_t>(v);
+}
+
+// Self-test of the bounded wait: nothing ever arrives on this barrier.
+__global__ void wait_timeout_selftest_kernel(uint64_t timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bar, 1);
+    abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  const bool ok = ptx::mbar_wait(&bar, 0, &abort_flag, timeout_ns);
+  if (!__all_sync(0xFFFFFFFFu, ok) && threadIdx.x == 0)
+    atomicCAS(&g_nvfp4_device_status, 0, NVFP4_ERR_DEVICE_TIMEOUT);
+}
+
+// ------------------------------------------------------------------------------------------
+// Host side
+// ------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(ptr);
+  }();
+  return fn;
+}
+
+bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                 uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr int kMaxDevices = 64;
+
+template <class C>
+int set_smem_attr_once(int dev) {
+  static std::once_flag flags[kMaxDevices];
+  static cudaError_t errs[kMaxDevices];
+  if (dev < 0 || dev >= kMaxDevices) return NVFP4_ERR_NO_DEVICE;
+  std::call_once(flags[dev], [&] {
+    errs[dev] = cudaFuncSetAttribute(gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::SMEM_ALLOC);
+  });
+  return status_from_cuda(errs[dev]);
+}
+
+using CfgWide = Cfg<256, 4, 1>;    // 128 x 256 tiles, 4-stage ring, one accumulator
+using CfgNarrow = Cfg<128, 6, 2>;  // 128 x 128 tiles, 6-stage ring, double-buffered accumulator
+
+template <class C>
+int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
+           const float* scale_ptr, float scale_val, void* D, int64_t M, int64_t N, int64_t K,
+           cudaStream_t stream) {
+  int dev = 0;
+  const int sms = current_device_sm_count(&dev);
+  if (sms <= 0) return NVFP4_ERR_NO_DEVICE;
+  int st = set_smem_attr_once<C>(dev);
+  if (st != NVFP4_OK) return st;
+
+  CUtensorMap tm_a, tm_b, tm_sfa, tm_sfb, tm_d;
+  const uint64_t kb = uint64_t(K) / 2, ks = uint64_t(K) / 16;
+  bool ok = make_map_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, kb, M, kb, kBKBytes, kBM,
+                        CU_TENSOR_MAP_SWIZZLE_128B) &&
+            make_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, B, kb, N, kb, kBKBytes, C::BN,
+                        CU_TENSOR_MAP_SWIZZLE_128B) &&
+            make_map_2d(&tm_sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, A_sf, ks, M, ks, kSfBytesPerRow,
+                        kBM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+            make_map_2d(&tm_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, B_sf, ks, N, ks, kSfBytesPerRow,
+                        C::BN, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+            make_map_2d(&tm_d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, D, N, M, uint64_t(N) * 2,
+                        kEpiCols, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (!ok) return encode_fn() ? NVFP4_ERR_INVALID_VALUE : NVFP4_ERR_NO_DEVICE;
+
+  Params p;
+  p.scale_ptr = scale_ptr;
+  p.scale_val = scale_val;
+  p.m = int(M);
+  p.n = int(N);
+  p.m_blocks = int((M + kBM - 1) / kBM);
+  p.n_blocks = int((N + C::BN - 1) / C::BN);
+  p.k_stages = int(K / kBK);
+  p.timeout_ns = 2000000000ull;  // 2 s per wait: far above any legitimate stall
+  const int64_t tiles = int64_t(p.m_blocks) * p.n_blocks;
+  const int grid = int(tiles < sms ? tiles : sms);
+  gemm_kernel<C><<<grid, kThreads, C::SMEM_ALLOC, stream>>>(tm_a, tm_b, tm_sfa, tm_sfb, tm_d, p);
+  return status_from_cuda(cudaGetLastError());
+}
+
+int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const float* scale_ptr,
+        float scale_val, void* D, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return NVFP4_ERR_INVALID_VALUE;
+  if (K % kBK != 0 || N % 8 != 0) return NVFP4_ERR_UNSUPPORTED_SHAPE;
+  if (M > 0x7FFFFFFF || N > 0x7FFFFFFF || K > 0x7FFFFFFF) return NVFP4_ERR_TOO_LARGE;
+  if (M == 0 || N == 0) return NVFP4_OK;
+  if (!D) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned_to(D, 16)) return NVFP4_ERR_MISALIGNED;
+  if (K == 0) {
+    fill_empty_k_kernel<<<148, 256, 0, stream>>>(static_cast<uint16_t*>(D), M * N, scale_ptr,
+                                                 scale_val);
+    return status_from_cuda(cudaGetLastError());
+  }
+  if (!A || !B || !A_sf || !B_sf) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned_to(A, 16) || !aligned_to(B, 16) || !aligned_to(A_sf, 16) || !aligned_to(B_sf, 16))
+    return NVFP4_ERR_MISALIGNED;
+  return launch<CfgWide>(A, B, A_sf, B_sf, scale_ptr, scale_val, D, M, N, K, stream);
+}
+
+}  // namespace gemm
+
+int current_device_sm_count(int* device_out) {
+  static int cache[gemm::kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= gemm::kMaxDevices) return -1;
+  if (device_out) *device_out = dev;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+}  // namespace nvfp4
+
+extern "C" {
+
+int nvfp4_gemm(const void* A, const void* B, const void* A_sf, const void* B_sf, const float* scale,
+               void* D, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  if (!scale) return NVFP4_ERR_INVALID_VALUE;
+  return nvfp4::gemm::run(A, B, A_sf, B_sf, scale, 0.0f, D, M, N, K, stream);
+}
+
+int nvfp4_gemm_host_scale(const void* A, const void* B, const void* A_sf, const void* B_sf,
+                          float scale, void* D, int64_t M, int64_t N, int64_t K,
+                          cudaStream_t stream) {
+  return nvfp4::gemm::run(A, B, A_sf, B_sf, nullptr, scale, D, M, N, K, stream);
+}
+
+int nvfp4_device_status(int* status_out, cudaStream_t stream) {
+  if (!status_out) return NVFP4_ERR_INVALID_VALUE;
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_nvfp4_device_status, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return NVFP4_ERR_CUDA;
+  *status_out = v;
+  return NVFP4_OK;
+}
+
+int nvfp4_clear_device_status(cudaStream_t stream) {
+  static const int zero = 0;
+  cudaError_t e = cudaMemcpyToSymbolAsync(g_nvfp4_device_status, &zero, sizeof(int), 0,
+                                          cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  return nvfp4::status_from_cuda(e);
+}
+
+int nvfp4_selftest_wait_timeout(uint64_t timeout_ns, cudaStream_t stream) {
+  nvfp4::gemm::wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(timeout_ns);
+  return nvfp4::status_from_cuda(cudaGetLastError());
+}
+
+const char* nvfp4_status_string(int status) {
+  switch (status) {
+    case NVFP4_OK: return "NVFP4_OK";
+    case NVFP4_ERR_INVALID_VALUE: return "NVFP4_ERR_INVALID_VALUE";
+    case NVFP4_ERR_UNSUPPORTED_SHAPE: return "NVFP4_ERR_UNSUPPORTED_SHAPE";
+    case NVFP4_ERR_MISALIGNED: return "NVFP4_ERR_MISALIGNED";
+    case NVFP4_ERR_CUDA: return "NVFP4_ERR_CUDA";
+    case NVFP4_ERR_NO_DEVICE: return "NVFP4_ERR_NO_DEVICE";
+    case NVFP4_ERR_DEVICE_TIMEOUT: return "NVFP4_ERR_DEVICE_TIMEOUT";
+    case NVFP4_ERR_TOO_LARGE: return "NVFP4_ERR_TOO_LARGE";
+    default: return "NVFP4_ERR_UNKNOWN";
+  }
+}
+
+int nvfp4_version(void) { return 0x000100; }
+
+}  // extern "C"

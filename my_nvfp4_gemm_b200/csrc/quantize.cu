@@ -1,0 +1,193 @@
+// quantize.cu — NVFP4 quantize (bf16 -> packed E2M1 + UE4M3 per 16) and dequantize kernels
+// for sm_100a, plus their C-ABI entry points.
+//
+// Arithmetic is the reference's, step for step (csrc/quantize/quantize_nvfp4.cu:6-62):
+//   amax  = NaN-propagating max of |x| over the 16-element block, seeded with bf16 0x0001
+//   sf    = e4m3_rn_satfinite((f32(amax) * s) * (1/6))
+//   os    = rcp_rn(f32(sf) * rcp_rn(s))
+//   q_i   = e2m1_rn_satfinite(f32(x_i) * os)
+//   deq_i = bf16_rn(f32(q_i) * (f32(sf) * rcp_rn(s)))
+// so the bytes are identical to the reference kernel's. The memory side is redesigned for B200
+// HBM3e: each thread owns half a block (8 bf16 = one 16-byte load), the block amax is finished
+// with one warp shuffle, every warp access is a contiguous 512 B (loads) / 128 B (packed
+// stores), four independent half-blocks per thread keep loads in flight, and the scale is read
+// from device memory so no host synchronisation is needed.
+#include <cstdint>
+
+#include "capi_util.h"
+#include "ptx.cuh"
+
+namespace nvfp4 {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;                                 // half-blocks per thread
+constexpr int64_t kHalfBlocksPerCta = int64_t(kThreads) * kUnroll;
+constexpr float kRcpE2m1Max = 1.0f / 6.0f;                 // 0.16666667f, as the reference
+
+__device__ __forceinline__ float bf16lo_to_f32(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi_to_f32(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+__device__ __forceinline__ uint32_t abs_max_bf16x2(uint32_t acc, uint32_t w) {
+  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&acc);
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&w);
+  __nv_bfloat162 r = __hmax2_nan(a, __habs2(b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t acc, uint32_t w) {
+  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&acc);
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&w);
+  __nv_bfloat162 r = __hmax2_nan(a, b);
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// One thread = one half-block of 8 bf16. Lanes 2j and 2j+1 hold the two halves of a block.
+template <bool kDeviceScale>
+__global__ void __launch_bounds__(kThreads)
+quantize_kernel(const uint4* __restrict__ x, const float* __restrict__ scale_ptr, float scale_val,
+                int64_t n_half_blocks, uint32_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  const float s = kDeviceScale ? __ldg(scale_ptr) : scale_val;
+  const float rcp_s = __frcp_rn(s);
+  const int64_t base = int64_t(blockIdx.x) * kHalfBlocksPerCta + threadIdx.x;
+
+  uint4 v[kUnroll];
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t h = base + int64_t(u) * kThreads;
+    v[u] = (h < n_half_blocks) ? ptx::ld_stream_v4(x + h) : make_uint4(0, 0, 0, 0);
+  }
+
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t h = base + int64_t(u) * kThreads;
+    uint32_t m = 0x00010001u;  // bf16x2 {0x0001, 0x0001}: the reference's non-zero floor
+    m = abs_max_bf16x2(m, v[u].x);
+    m = abs_max_bf16x2(m, v[u].y);
+    m = abs_max_bf16x2(m, v[u].z);
+    m = abs_max_bf16x2(m, v[u].w);
+    m = max_bf16x2(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));  // other half of the block
+    const __nv_bfloat162 m2 = *reinterpret_cast<__nv_bfloat162*>(&m);
+    const float amax = __bfloat162float(__hmax_nan(m2.x, m2.y));
+
+    const float t = __fmul_rn(__fmul_rn(amax, s), kRcpE2m1Max);
+    const uint8_t sfb = static_cast<uint8_t>(ptx::f32x2_to_e4m3x2(t, 0.0f) & 0xFFu);
+    const float os = __frcp_rn(__fmul_rn(ptx::e4m3_to_f32(sfb), rcp_s));
+
+    const uint32_t packed = ptx::f32x8_to_e2m1x8(
+        __fmul_rn(bf16lo_to_f32(v[u].x), os), __fmul_rn(bf16hi_to_f32(v[u].x), os),
+        __fmul_rn(bf16lo_to_f32(v[u].y), os), __fmul_rn(bf16hi_to_f32(v[u].y), os),
+        __fmul_rn(bf16lo_to_f32(v[u].z), os), __fmul_rn(bf16hi_to_f32(v[u].z), os),
+        __fmul_rn(bf16lo_to_f32(v[u].w), os), __fmul_rn(bf16hi_to_f32(v[u].w), os));
+    if (h < n_half_blocks) {
+      q[h] = packed;
+      if ((h & 1) == 0) sf[h >> 1] = sfb;
+    }
+  }
+}
+
+// One thread = one half-block: 4 packed bytes + the block's scale byte -> 8 bf16 (16 bytes).
+template <bool kDeviceScale>
+__global__ void __launch_bounds__(kThreads)
+dequantize_kernel(const uint32_t* __restrict__ q, const float* __restrict__ scale_ptr,
+                  float scale_val, const uint8_t* __restrict__ sf, int64_t n_half_blocks,
+                  uint4* __restrict__ y) {
+  const float s = kDeviceScale ? __ldg(scale_ptr) : scale_val;
+  const float rcp_s = __frcp_rn(s);
+  const int64_t base = int64_t(blockIdx.x) * kHalfBlocksPerCta + threadIdx.x;
+
+  uint32_t w[kUnroll];
+  uint8_t sb[kUnroll];
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t h = base + int64_t(u) * kThreads;
+    const bool in = h < n_half_blocks;
+    w[u] = in ? ptx::ld_stream_u32(q + h) : 0u;
+    sb[u] = in ? ptx::ld_nc_u8(sf + (h >> 1)) : uint8_t(0);
+  }
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t h = base + int64_t(u) * kThreads;
+    const float scale = __fmul_rn(ptx::e4m3_to_f32(sb[u]), rcp_s);
+    uint32_t hf[4];
+    ptx::e2m1x8_to_f16x8(w[u], hf);
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 p = *reinterpret_cast<const __half2*>(&hf[i]);
+      o[i] = ptx::f32x2_to_bf16x2(__fmul_rn(__low2float(p), scale),
+                                  __fmul_rn(__high2float(p), scale));
+    }
+    if (h < n_half_blocks) ptx::st_v4(y + h, make_uint4(o[0], o[1], o[2], o[3]));
+  }
+}
+
+int launch_quantize(const void* input, const float* scale_ptr, float scale_val, int64_t numel,
+                    void* output, void* output_sf, cudaStream_t stream) {
+  if (numel < 0) return NVFP4_ERR_INVALID_VALUE;
+  if (numel % 16 != 0) return NVFP4_ERR_UNSUPPORTED_SHAPE;
+  if (numel == 0) return NVFP4_OK;
+  if (!input || !output || !output_sf) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned_to(input, 16) || !aligned_to(output, 4)) return NVFP4_ERR_MISALIGNED;
+  const int64_t n_half = numel / 8;
+  const int64_t grid = (n_half + kHalfBlocksPerCta - 1) / kHalfBlocksPerCta;
+  if (grid > 0x7FFFFFFF) return NVFP4_ERR_TOO_LARGE;
+  if (scale_ptr)
+    quantize_kernel<true><<<unsigned(grid), kThreads, 0, stream>>>(
+        static_cast<const uint4*>(input), scale_ptr, 0.0f, n_half,
+        static_cast<uint32_t*>(output), static_cast<uint8_t*>(output_sf));
+  else
+    quantize_kernel<false><<<unsigned(grid), kThreads, 0, stream>>>(
+        static_cast<const uint4*>(input), nullptr, scale_val, n_half,
+        static_cast<uint32_t*>(output), static_cast<uint8_t*>(output_sf));
+  return status_from_cuda(cudaGetLastError());
+}
+
+int launch_dequantize(const void* input, const float* scale_ptr, float scale_val,
+                      const void* input_sf, int64_t n_bytes, void* output, cudaStream_t stream) {
+  if (n_bytes < 0) return NVFP4_ERR_INVALID_VALUE;
+  if (n_bytes % 8 != 0) return NVFP4_ERR_UNSUPPORTED_SHAPE;
+  if (n_bytes == 0) return NVFP4_OK;
+  if (!input || !input_sf || !output) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned_to(input, 4) || !aligned_to(output, 16)) return NVFP4_ERR_MISALIGNED;
+  const int64_t n_half = n_bytes / 4;
+  const int64_t grid = (n_half + kHalfBlocksPerCta - 1) / kHalfBlocksPerCta;
+  if (grid > 0x7FFFFFFF) return NVFP4_ERR_TOO_LARGE;
+  if (scale_ptr)
+    dequantize_kernel<true><<<unsigned(grid), kThreads, 0, stream>>>(
+        static_cast<const uint32_t*>(input), scale_ptr, 0.0f,
+        static_cast<const uint8_t*>(input_sf), n_half, static_cast<uint4*>(output));
+  else
+    dequantize_kernel<false><<<unsigned(grid), kThreads, 0, stream>>>(
+        static_cast<const uint32_t*>(input), nullptr, scale_val,
+        static_cast<const uint8_t*>(input_sf), n_half, static_cast<uint4*>(output));
+  return status_from_cuda(cudaGetLastError());
+}
+
+}  // namespace
+}  // namespace nvfp4
+
+extern "C" {
+
+int nvfp4_quantize(const void* input, const float* input_scale, int64_t numel, void* output,
+                   void* output_sf, cudaStream_t stream) {
+  if (!input_scale) return NVFP4_ERR_INVALID_VALUE;
+  return nvfp4::launch_quantize(input, input_scale, 0.0f, numel, output, output_sf, stream);
+}
+
+int nvfp4_quantize_host_scale(const void* input, float input_scale, int64_t numel, void* output,
+                              void* output_sf, cudaStream_t stream) {
+  return nvfp4::launch_quantize(input, nullptr, input_scale, numel, output, output_sf, stream);
+}
+
+int nvfp4_dequantize(const void* input, const float* input_scale, const void* input_sf,
+                     int64_t n_bytes, void* output, cudaStream_t stream) {
+  if (!input_scale) return NVFP4_ERR_INVALID_VALUE;
+  return nvfp4::launch_dequantize(input, input_scale, 0.0f, input_sf, n_bytes, output, stream);
+}
+
+int nvfp4_dequantize_host_scale(const void* input, float input_scale, const void* input_sf,
+                                int64_t n_bytes, void* output, cudaStream_t stream) {
+  return nvfp4::launch_dequantize(input, nullptr, input_scale, input_sf, n_bytes, output, stream);
+}
+
+}  // extern "C"

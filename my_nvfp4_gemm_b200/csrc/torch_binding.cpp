@@ -1,0 +1,175 @@
+// torch_binding.cpp — the `my_plugins` Python module: the reference plugin's three functions
+// with the same names, argument order, tensor types/shapes and error behaviour (TORCH_CHECK ->
+// RuntimeError), implemented on top of the C ABI of libnvfp4_b200.so.
+//
+//   quantize_nvfp4(input, input_scale)            csrc/quantize/quantize_nvfp4_bindling.cpp:4-20
+//   de_quantize_nvfp4(input, input_scale, sf)     csrc/quantize/quantize_nvfp4_bindling.cpp:23-37
+//   gemm_nvfp4(A, B, A_sf, B_sf, scale)           csrc/gemm/gemm_nvfp4_bindling.cpp:4-25
+//
+// Differences, all on the side of the reference's undefined behaviour:
+//   * a CUDA scale tensor is passed to the kernels by device pointer: no .item() device->host
+//     synchronisation per call (a CPU scale tensor is read on the host, also without a sync);
+//   * shapes the reference silently mis-handles or aborts on are rejected with RuntimeError:
+//     last dim % 16 (quantize), sf shape mismatches, K mismatch between A and B, K % 256 and
+//     N % 8 (the reference assert()s, gemm_nvfp4.cu:246);
+//   * sizes are 64-bit.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "../../include/nvfp4_b200.h"
+
+namespace {
+
+void check_status(int st, const char* what) {
+  TORCH_CHECK(st == NVFP4_OK, what, " failed: ", nvfp4_status_string(st));
+}
+
+struct ScaleArg {
+  const float* dev = nullptr;
+  float host = 0.0f;
+};
+
+ScaleArg scale_arg(const torch::Tensor& s, const torch::Device& data_device, const char* name) {
+  TORCH_CHECK(s.dtype() == torch::kFloat32 && 0 == s.dim(), name, " must be float32 and scalar");
+  ScaleArg a;
+  if (s.is_cuda()) {
+    TORCH_CHECK(s.device() == data_device, name, " must be on the same device as the data (",
+                data_device, "), got ", s.device());
+    a.dev = s.data_ptr<float>();
+  } else {
+    TORCH_CHECK(s.device().is_cpu(), name, " must be a CPU or CUDA tensor");
+    a.host = *s.data_ptr<float>();
+  }
+  return a;
+}
+
+std::tuple<torch::Tensor, torch::Tensor> py_quantize_nvfp4(const torch::Tensor& input,
+                                                           const torch::Tensor& input_scale) {
+  TORCH_CHECK(input.dtype() == torch::kBFloat16 && input.is_contiguous(),
+              "input must be bf16 and contiguous");
+  TORCH_CHECK(input_scale.dtype() == torch::kFloat32 && 0 == input_scale.dim(),
+              "input_scale must be float32 and scalar");
+  TORCH_CHECK(input.device().is_cuda(), "input must be on cuda device");
+  TORCH_CHECK(input.dim() >= 1 && input.size(-1) % 16 == 0,
+              "input's last dimension must be a multiple of 16, got ", input.sizes());
+  const c10::cuda::CUDAGuard guard(input.device());
+  const ScaleArg sc = scale_arg(input_scale, input.device(), "input_scale");
+
+  auto out_sizes = input.sizes().vec();
+  auto sf_sizes = input.sizes().vec();
+  out_sizes.back() /= 2;
+  sf_sizes.back() /= 16;
+  auto output = torch::empty(out_sizes, torch::dtype(torch::kUInt8).device(input.device()));
+  auto output_sf = torch::empty(sf_sizes, torch::dtype(torch::kFloat8_e4m3fn).device(input.device()));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(input.device().index());
+  const int st = sc.dev ? nvfp4_quantize(input.data_ptr(), sc.dev, input.numel(), output.data_ptr(),
+                                         output_sf.data_ptr(), stream)
+                        : nvfp4_quantize_host_scale(input.data_ptr(), sc.host, input.numel(),
+                                                    output.data_ptr(), output_sf.data_ptr(), stream);
+  check_status(st, "quantize_nvfp4");
+  return std::make_tuple(output, output_sf);
+}
+
+torch::Tensor py_de_quantize_nvfp4(const torch::Tensor& input, const torch::Tensor& input_scale,
+                                   const torch::Tensor& input_sf) {
+  TORCH_CHECK(input.dtype() == torch::kUInt8 && input.is_contiguous(),
+              "input must be uint8 and contiguous");
+  TORCH_CHECK(input_scale.dtype() == torch::kFloat32 && 0 == input_scale.dim(),
+              "input_scale must be float32 and scalar");
+  TORCH_CHECK(input_sf.dtype() == torch::kFloat8_e4m3fn && input_sf.is_contiguous(),
+              "input_sf must be float8_e4m3 and contiguous");
+  TORCH_CHECK(input.device().is_cuda() && input_sf.device().is_cuda(),
+              "input&input_sf must be on cuda device");
+  TORCH_CHECK(input_sf.device() == input.device(), "input_sf must be on the input's device");
+  TORCH_CHECK(input.dim() >= 1 && input.size(-1) % 8 == 0,
+              "input's last dimension must be a multiple of 8 (16 elements per scale), got ",
+              input.sizes());
+  TORCH_CHECK(input_sf.numel() * 8 == input.numel(), "input_sf has ", input_sf.numel(),
+              " scale factors, expected ", input.numel() / 8);
+  const c10::cuda::CUDAGuard guard(input.device());
+  const ScaleArg sc = scale_arg(input_scale, input.device(), "input_scale");
+
+  auto out_sizes = input.sizes().vec();
+  out_sizes.back() *= 2;
+  auto output = torch::empty(out_sizes, torch::dtype(torch::kBFloat16).device(input.device()));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(input.device().index());
+  const int st =
+      sc.dev ? nvfp4_dequantize(input.data_ptr(), sc.dev, input_sf.data_ptr(), input.numel(),
+                                output.data_ptr(), stream)
+             : nvfp4_dequantize_host_scale(input.data_ptr(), sc.host, input_sf.data_ptr(),
+                                           input.numel(), output.data_ptr(), stream);
+  check_status(st, "de_quantize_nvfp4");
+  return output;
+}
+
+torch::Tensor py_gemm_nvfp4(const torch::Tensor& A, const torch::Tensor& B,
+                            const torch::Tensor& A_sf, const torch::Tensor& B_sf,
+                            const torch::Tensor& scale) {
+  TORCH_CHECK(A.dtype() == torch::kUInt8 && A.is_contiguous(), "A must be uint8 and contiguous");
+  TORCH_CHECK(B.dtype() == torch::kUInt8 && B.is_contiguous(), "B must be uint8 and contiguous");
+  TORCH_CHECK(2 == A.dim() && 2 == B.dim(), "A and B must be 2D");
+  TORCH_CHECK(A_sf.dtype() == torch::kFloat8_e4m3fn && A_sf.is_contiguous(),
+              "A_sf must be float8_e4m3 and contiguous");
+  TORCH_CHECK(B_sf.dtype() == torch::kFloat8_e4m3fn && B_sf.is_contiguous(),
+              "B_sf must be float8_e4m3 and contiguous");
+  TORCH_CHECK(scale.dtype() == torch::kFloat32 && 0 == scale.dim(),
+              "scale must be float32 and scalar");
+  TORCH_CHECK(A.device().is_cuda() && B.device().is_cuda() && A_sf.device().is_cuda() &&
+                  B_sf.device().is_cuda(),
+              "A&B&A_sf&B_sf must be on cuda device");
+  TORCH_CHECK(B.device() == A.device() && A_sf.device() == A.device() &&
+                  B_sf.device() == A.device(),
+              "A, B, A_sf and B_sf must be on the same device");
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1) * 2;
+  TORCH_CHECK(B.size(1) * 2 == K, "A and B must have the same K: A is ", A.sizes(), ", B is ",
+              B.sizes());
+  TORCH_CHECK(K % 256 == 0, "K must be a multiple of 256, got ", K);
+  TORCH_CHECK(N % 8 == 0, "N must be a multiple of 8, got ", N);
+  TORCH_CHECK(A_sf.numel() == M * (K / 16) && (A_sf.dim() < 2 || A_sf.size(0) == M),
+              "A_sf must hold [M, K/16] = [", M, ", ", K / 16, "] scale factors, got ",
+              A_sf.sizes());
+  TORCH_CHECK(B_sf.numel() == N * (K / 16) && (B_sf.dim() < 2 || B_sf.size(0) == N),
+              "B_sf must hold [N, K/16] = [", N, ", ", K / 16, "] scale factors, got ",
+              B_sf.sizes());
+  const c10::cuda::CUDAGuard guard(A.device());
+  const ScaleArg sc = scale_arg(scale, A.device(), "scale");
+
+  auto D = torch::empty({M, N}, torch::dtype(torch::kBFloat16).device(A.device()));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(A.device().index());
+  const int st = sc.dev ? nvfp4_gemm(A.data_ptr(), B.data_ptr(), A_sf.data_ptr(), B_sf.data_ptr(),
+                                     sc.dev, D.data_ptr(), M, N, K, stream)
+                        : nvfp4_gemm_host_scale(A.data_ptr(), B.data_ptr(), A_sf.data_ptr(),
+                                                B_sf.data_ptr(), sc.host, D.data_ptr(), M, N, K,
+                                                stream);
+  check_status(st, "gemm_nvfp4");
+  return D;
+}
+
+// Device status word of the library on the current CUDA device (synchronises the stream).
+int64_t py_device_status() {
+  int v = 0;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(nvfp4_device_status(&v, stream), "device_status");
+  return v;
+}
+
+void py_clear_device_status() {
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_status(nvfp4_clear_device_status(stream), "clear_device_status");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(my_plugins, m) {
+  m.doc() = "my_plugins: NVFP4 quantize / dequantize / GEMM for B200 (sm_100a)";
+  m.def("quantize_nvfp4", &py_quantize_nvfp4, "quantize_nvfp4", py::arg("input"),
+        py::arg("input_scale"));
+  m.def("de_quantize_nvfp4", &py_de_quantize_nvfp4, "de_quantize_nvfp4", py::arg("input"),
+        py::arg("input_scale"), py::arg("input_sf"));
+  m.def("gemm_nvfp4", &py_gemm_nvfp4, "gemm_nvfp4", py::arg("A"), py::arg("B"), py::arg("A_sf"),
+        py::arg("B_sf"), py::arg("scale"));
+  m.def("device_status", &py_device_status,
+        "status word of the library's kernels on the current device (0 = OK)");
+  m.def("clear_device_status", &py_clear_device_status, "reset the device status word to 0");
+}
