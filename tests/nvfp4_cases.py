@@ -10,10 +10,11 @@ import numpy as np
 def f32_to_bf16_bits(x) -> np.ndarray:
     """Round-to-nearest-even fp32 -> bf16 bits (NaN -> 0x7FC0, as torch does)."""
     x = np.asarray(x, dtype=np.float32)
-    u = x.view(np.uint32).astype(np.uint64)
+    flat = x.reshape(-1)
+    u = flat.view(np.uint32).astype(np.uint64)
     r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
-    r[np.isnan(x)] = 0x7FC0
-    return r
+    r[np.isnan(flat)] = 0x7FC0
+    return r.reshape(x.shape)
 
 
 def bf16_bits_to_f32(h) -> np.ndarray:
