@@ -8,17 +8,18 @@
 // mma.sync design does not exist on sm_100a and is not followed. This kernel is:
 //
 //   * persistent: one CTA per SM walks output tiles of 128 x BN (BN = 256 or 128);
-//   * warp-specialised (256 threads):
-//       warp 0  TMA producer: A/B tiles (128B-swizzled) and scale-factor tiles into a
+//   * warp-specialised (320 threads):
+//       warp 8  TMA producer: A/B tiles (128B-swizzled) and scale-factor tiles into a
 //               STAGES-deep shared-memory ring, guarded by full and empty mbarriers;
-//       warp 1  MMA issuer: owns the tensor-memory allocation, copies the stage's scale factors
-//               into TMEM (tcgen05.cp) and issues tcgen05.mma .kind::mxf4nvf4
-//               .block_scale.scale_vec::4X (M=128, N=BN, K=64) into a TMEM fp32 accumulator;
-//       warp 2  scale-factor transposer: the API's row-major scale factors are rearranged in
-//               shared memory into the 32-lane x 4-column chunks the MMA reads from TMEM;
-//       warps 4-7 epilogue: tcgen05.ld of the accumulator, x (1/scale), bf16 convert, staged
-//               through 64B-swizzled shared memory and written with TMA tensor stores
-//               (bounds-clipped, so ragged M and N need no masking);
+//       warps 0-3 scale-factor writers: read the API's row-major UE4M3 factors from shared
+//               memory and write them with tcgen05.st into the stage's tensor-memory slot, in
+//               the lane/column layout the block-scaled MMA reads (one warp per lane quarter);
+//       warp 9  MMA issuer: owns the tensor-memory allocation and issues tcgen05.mma
+//               .kind::mxf4nvf4.block_scale.scale_vec::4X (M=128, N=BN, K=64) into a TMEM fp32
+//               accumulator;
+//       warps 4-7 epilogue: tcgen05.ld of the accumulator, x (1/scale), bf16 convert in
+//               registers, release of TMEM, then 64B-swizzled shared-memory staging and TMA
+//               tensor stores (bounds-clipped, so ragged M and N need no masking);
 //   * fault-safe: every mbarrier wait is bounded; a wait that times out raises a CTA-wide abort
 //     flag, every role returns, copies and MMAs in flight are drained (bounded), TMEM is freed,
 //     and NVFP4_ERR_DEVICE_TIMEOUT is recorded in the device status word.
@@ -41,8 +42,12 @@ constexpr int kBKBytes = kBK / 2;
 constexpr int kUmmaK = 64;          // K per tcgen05.mma kind::mxf4nvf4
 constexpr int kKSteps = kBK / kUmmaK;
 constexpr int kSfBytesPerRow = kBK / 16;  // 16 scale bytes per row per stage
-constexpr int kThreads = 256;
+constexpr int kNumSfWarps = 4;            // warps 0-3: scale-factor writers (TMEM quarters 0-3)
+constexpr int kFirstEpiWarp = 4;          // warps 4-7: epilogue (TMEM quarters 0-3)
 constexpr int kNumEpiWarps = 4;
+constexpr int kProducerWarp = 8;          // TMA producer
+constexpr int kMmaWarp = 9;               // MMA issuer, owns the TMEM allocation
+constexpr int kThreads = 32 * 10;
 constexpr int kEpiCols = 32;              // accumulator columns per epilogue store
 constexpr int kEpiBufBytes = 32 * kEpiCols * 2;  // 32 rows x 32 bf16 per epilogue warp
 
@@ -71,12 +76,14 @@ struct Cfg {
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;     // slack to align the base to 1 KiB
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget exceeded");
 
-  // Tensor memory columns: accumulators, then per-K-step scale-factor chunks.
+  // Tensor memory columns: accumulators, then one scale-factor slot per pipeline stage, so the
+  // factors of stage s+1 are written while the MMAs of stage s still read theirs. Within a slot:
+  // B's factors for K-steps 0..3 (BN/32 columns each), then A's (4 columns each).
   static constexpr uint32_t SFA_COLS_PER_STEP = 4;          // 128 rows -> one 32x4 chunk
   static constexpr uint32_t SFB_COLS_PER_STEP = BN / 32;    // BN/128 chunks of 4 columns
-  static constexpr uint32_t COL_SFA = BN * ACC_STAGES;
-  static constexpr uint32_t COL_SFB = COL_SFA + kKSteps * SFA_COLS_PER_STEP;
-  static constexpr uint32_t COLS_USED = COL_SFB + kKSteps * SFB_COLS_PER_STEP;
+  static constexpr uint32_t SF_SLOT_COLS = kKSteps * (SFA_COLS_PER_STEP + SFB_COLS_PER_STEP);
+  static constexpr uint32_t COL_SF = BN * ACC_STAGES;
+  static constexpr uint32_t COLS_USED = COL_SF + STAGES * SF_SLOT_COLS;
   static constexpr uint32_t TMEM_COLS = COLS_USED <= 32 ? 32 : COLS_USED <= 64 ? 64
                                       : COLS_USED <= 128 ? 128 : COLS_USED <= 256 ? 256 : 512;
   static_assert(COLS_USED <= 512, "tensor memory budget exceeded");
@@ -93,21 +100,41 @@ struct Params {
   uint64_t timeout_ns;
 };
 
-// In-place rearrangement of one 128-row scale-factor chunk held row-major (row r at r*16 bytes,
-// 4-byte word j = the 4 scale factors of K-step j) into four 512-byte chunks, one per K-step j,
-// each laid out as 32 rows x 16 bytes where row r holds step j's word of rows r, r+32, r+64,
-// r+96. tcgen05.cp .32x128b.warpx4 copies such a chunk into TMEM (lane r, columns c..c+3) and
-// replicates it into the four lane quarters, which is where the block-scaled MMA reads the
-// scale factor of row 32*q + r (column c + q). Executed by one full warp; conflict-free.
-__device__ __forceinline__ void transpose_sf_chunk(uint32_t base, int lane) {
-  uint4 w[4];
+// Scale-factor writer (one warp per TMEM lane quarter q). The block-scaled MMA of sub-partition
+// q reads the scale factors of A row 32q+r from TMEM lane 32q+r, column sfa+q, and those of B
+// row n from lane 32q+(n%32), column sfb+n/32 (B's factors are needed by every quarter). The
+// warp reads its rows' row-major factors from the stage's shared-memory tile (16 bytes per row
+// = K-steps 0..3) and writes its quarter of the stage's TMEM slot with tcgen05.st:
+//   slot + j*(BN/32) + i   <- step-j word of B row 32i + lane     (BN/8 columns)
+//   slot + BN/8 + 4j + k   <- step-j word of A row 32q + lane     (16 columns, k = 0..3)
+template <class C>
+__device__ __forceinline__ void write_sf_slot(uint32_t slot, uint32_t sfa_s, uint32_t sfb_s, int q,
+                                              int lane) {
+  constexpr int kChunksB = C::BN / 32;
+  uint32_t vb[C::BN / 8];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) w[q] = ptx::ld_shared_v4(base + (32 * q + lane) * 16);
-  __syncwarp();
-  ptx::st_shared_v4(base + 0 * 512 + lane * 16, make_uint4(w[0].x, w[1].x, w[2].x, w[3].x));
-  ptx::st_shared_v4(base + 1 * 512 + lane * 16, make_uint4(w[0].y, w[1].y, w[2].y, w[3].y));
-  ptx::st_shared_v4(base + 2 * 512 + lane * 16, make_uint4(w[0].z, w[1].z, w[2].z, w[3].z));
-  ptx::st_shared_v4(base + 3 * 512 + lane * 16, make_uint4(w[0].w, w[1].w, w[2].w, w[3].w));
+  for (int i = 0; i < kChunksB; ++i) {
+    const uint4 w = ptx::ld_shared_v4(sfb_s + uint32_t(32 * i + lane) * 16);
+    vb[0 * kChunksB + i] = w.x;
+    vb[1 * kChunksB + i] = w.y;
+    vb[2 * kChunksB + i] = w.z;
+    vb[3 * kChunksB + i] = w.w;
+  }
+  const uint4 a = ptx::ld_shared_v4(sfa_s + uint32_t(32 * q + lane) * 16);
+  uint32_t va[16];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    va[0 + k] = a.x;
+    va[4 + k] = a.y;
+    va[8 + k] = a.z;
+    va[12 + k] = a.w;
+  }
+  if constexpr (C::BN == 256) {
+    ptx::tmem_st_32x32b_x32(slot, vb);
+  } else {
+    ptx::tmem_st_32x32b_x16(slot, vb);
+  }
+  ptx::tmem_st_32x32b_x16(slot + C::BN / 8, va);
 }
 
 template <class C>
@@ -124,8 +151,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   uint8_t* sSFB = smem + C::OFF_SFB;
   uint8_t* sEPI = smem + C::OFF_EPI;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* full_bar = bars;                                  // TMA -> transposer
-  uint64_t* sf_bar = bars + C::STAGES;                        // transposer -> MMA
+  uint64_t* full_bar = bars;                                  // TMA -> scale-factor writers
+  uint64_t* sf_bar = bars + C::STAGES;                        // scale-factor writers -> MMA
   uint64_t* empty_bar = bars + 2 * C::STAGES;                 // MMA (commit) -> TMA
   uint64_t* tfull_bar = bars + 3 * C::STAGES;                 // MMA (commit) -> epilogue
   uint64_t* tempty_bar = tfull_bar + C::ACC_STAGES;           // epilogue -> MMA
@@ -140,7 +167,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
       ptx::mbar_init(&full_bar[i], 1);
-      ptx::mbar_init(&sf_bar[i], 1);
+      ptx::mbar_init(&sf_bar[i], kNumSfWarps);
       ptx::mbar_init(&empty_bar[i], 1);
     }
     for (int i = 0; i < C::ACC_STAGES; ++i) {
@@ -151,14 +178,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
+  if (warp == kProducerWarp && lane == 0) {
     ptx::tma_prefetch_desc(&tm_a);
     ptx::tma_prefetch_desc(&tm_b);
     ptx::tma_prefetch_desc(&tm_sfa);
     ptx::tma_prefetch_desc(&tm_sfb);
     ptx::tma_prefetch_desc(&tm_d);
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
     ptx::tmem_relinquish_alloc_permit();
   }
@@ -167,7 +194,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   ptx::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       int stage = 0;
@@ -200,7 +227,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = ptx::make_idesc_mxf4nvf4(kBM, C::BN);
@@ -216,19 +243,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
           if (!ptx::mbar_wait(&sf_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
           if (!ptx::mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
           ptx::tc_fence_after_sync();
-          const uint32_t sfa_s = ptx::smem_u32(sSFA + stage * C::SFA_STAGE);
-          const uint32_t sfb_s = ptx::smem_u32(sSFB + stage * C::SFB_STAGE);
-#pragma unroll
-          for (int j = 0; j < kKSteps; ++j)
-            ptx::tc_cp_32x128b_warpx4(tmem_base + C::COL_SFA + j * C::SFA_COLS_PER_STEP,
-                                      ptx::make_smem_desc(sfa_s + j * 512, 0, 128, ptx::kLayoutNone));
-#pragma unroll
-          for (int c = 0; c < C::BN / 128; ++c)
-#pragma unroll
-            for (int j = 0; j < kKSteps; ++j)
-              ptx::tc_cp_32x128b_warpx4(
-                  tmem_base + C::COL_SFB + j * C::SFB_COLS_PER_STEP + 4 * c,
-                  ptx::make_smem_desc(sfb_s + c * 2048 + j * 512, 0, 128, ptx::kLayoutNone));
+          const uint32_t t_sfb = tmem_base + C::COL_SF + uint32_t(stage) * C::SF_SLOT_COLS;
+          const uint32_t t_sfa = t_sfb + C::BN / 8;
           const uint32_t a_s = ptx::smem_u32(sA + stage * C::A_STAGE);
           const uint32_t b_s = ptx::smem_u32(sB + stage * C::B_STAGE);
 #pragma unroll
@@ -236,12 +252,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
             // K-step j starts 32 bytes further along the 128-byte swizzled rows.
             const uint64_t a_desc = ptx::make_smem_desc(a_s + j * 32, 0, 1024, ptx::kLayoutSW128);
             const uint64_t b_desc = ptx::make_smem_desc(b_s + j * 32, 0, 1024, ptx::kLayoutSW128);
-            ptx::tc_mma_mxf4nvf4(d_tmem, a_desc, b_desc, idesc,
-                                 tmem_base + C::COL_SFA + j * C::SFA_COLS_PER_STEP,
-                                 tmem_base + C::COL_SFB + j * C::SFB_COLS_PER_STEP,
-                                 (kb | j) != 0 ? 1u : 0u);
+            ptx::tc_mma_mxf4nvf4(d_tmem, a_desc, b_desc, idesc, t_sfa + 4 * j,
+                                 t_sfb + j * (C::BN / 32), (kb | j) != 0 ? 1u : 0u);
           }
-          ptx::tc_commit(&empty_bar[stage]);  // frees the smem slot once these MMAs are done
+          ptx::tc_commit(&empty_bar[stage]);  // frees the smem slot and its TMEM scale slot
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
         }
         ptx::tc_commit(&tfull_bar[acc]);      // accumulator ready for the epilogue
@@ -255,28 +269,32 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         ptx::mbar_wait(drain_bar, 0, &no_abort, p.timeout_ns);
       }
     }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------------ scale-factor transposer
+  } else if (warp < kNumSfWarps) {
+    // ------------------------------------------------------------------ scale-factor writers
+    // Stage s's TMEM slot is rewritten only after full[s] of its next fill, which the producer
+    // issues after empty[s]: the MMAs that read the slot's previous contents have completed.
+    const int q = warp;
+    const uint32_t lane_base = uint32_t(q * 32) << 16;
     int stage = 0;
     uint32_t phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       for (int kb = 0; kb < p.k_stages; ++kb) {
         const bool ok = ptx::mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns);
-        if (!__all_sync(0xFFFFFFFFu, ok)) goto transposer_done;
-        transpose_sf_chunk(ptx::smem_u32(sSFA + stage * C::SFA_STAGE), lane);
-#pragma unroll
-        for (int c = 0; c < C::BN / 128; ++c)
-          transpose_sf_chunk(ptx::smem_u32(sSFB + stage * C::SFB_STAGE + c * 2048), lane);
-        ptx::fence_proxy_async_smem();  // generic-proxy writes -> visible to tcgen05.cp
+        if (!__all_sync(0xFFFFFFFFu, ok)) goto sf_done;
+        write_sf_slot<C>(tmem_base + lane_base + C::COL_SF + uint32_t(stage) * C::SF_SLOT_COLS,
+                         ptx::smem_u32(sSFA + stage * C::SFA_STAGE),
+                         ptx::smem_u32(sSFB + stage * C::SFB_STAGE), q, lane);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&sf_bar[stage]);
         if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
       }
     }
-  transposer_done:;
-  } else if (warp >= 4) {
+  sf_done:;
+  } else if (warp >= kFirstEpiWarp && warp < kFirstEpiWarp + kNumEpiWarps) {
     // ------------------------------------------------------------------ epilogue
-    const int ew = warp - 4;  // == warp % 4: this warp may access TMEM lanes 32*ew .. 32*ew+31
+    const int ew = warp - kFirstEpiWarp;  // == warp % 4: TMEM lanes 32*ew .. 32*ew+31
     const float scale = p.scale_ptr ? __ldg(p.scale_ptr) : p.scale_val;
     const float alpha = __frcp_rn(scale);
     uint8_t* buf = sEPI + ew * kEpiBufBytes;
@@ -291,29 +309,37 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
       ptx::tc_fence_after_sync();
       const uint32_t t_row = tmem_base + (uint32_t(ew * 32) << 16) + uint32_t(acc * C::BN);
-#pragma unroll 1
-      for (int c = 0; c < C::BN / kEpiCols; ++c) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(t_row + c * kEpiCols, r);
-        ptx::tmem_wait_ld();
-        if (c == C::BN / kEpiCols - 1) {
-          // The whole accumulator is in registers: hand TMEM back to the MMA warp.
-          ptx::tc_fence_before_sync();
-          __syncwarp();
-          if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
-        }
-        uint32_t o[16];
+      // Drain this thread's accumulator row into registers as bf16 pairs, 64 columns per
+      // tcgen05.wait::ld, then hand TMEM back to the MMA warp at once: the next tile's MMAs
+      // overlap the shared-memory staging and TMA stores below.
+      uint32_t pk[C::BN / 2];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          o[i] = ptx::f32x2_to_bf16x2(__uint_as_float(r[2 * i]) * alpha,
-                                      __uint_as_float(r[2 * i + 1]) * alpha);
+      for (int g = 0; g < C::BN / 64; ++g) {
+        uint32_t r0[32], r1[32];
+        ptx::tmem_ld_32x32b_x32(t_row + g * 64, r0);
+        ptx::tmem_ld_32x32b_x32(t_row + g * 64 + 32, r1);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          pk[g * 32 + i] = ptx::f32x2_to_bf16x2(__uint_as_float(r0[2 * i]) * alpha,
+                                                __uint_as_float(r0[2 * i + 1]) * alpha);
+          pk[g * 32 + 16 + i] = ptx::f32x2_to_bf16x2(__uint_as_float(r1[2 * i]) * alpha,
+                                                     __uint_as_float(r1[2 * i + 1]) * alpha);
+        }
+      }
+      ptx::tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+#pragma unroll
+      for (int c = 0; c < C::BN / kEpiCols; ++c) {
         if (lane == 0) ptx::bulk_wait_group_read<0>();  // previous store has read the buffer
         __syncwarp();
         const uint32_t row = buf_s + uint32_t(lane) * 64;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           ptx::st_shared_v4(row + ((uint32_t(k) ^ swz) << 4),
-                            make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]));
+                            make_uint4(pk[c * 16 + 4 * k], pk[c * 16 + 4 * k + 1],
+                                       pk[c * 16 + 4 * k + 2], pk[c * 16 + 4 * k + 3]));
         ptx::fence_proxy_async_smem();
         __syncwarp();
         // Boxes that start inside D are clipped by the TMA unit; boxes entirely outside
@@ -331,7 +357,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   ptx::tc_fence_before_sync();
   __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) atomicCAS(&g_nvfp4_device_status, 0, NVFP4_ERR_DEVICE_TIMEOUT);
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     __syncwarp();
     ptx::tc_fence_after_sync();
     ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
