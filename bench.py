@@ -87,7 +87,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
         return self
@@ -196,6 +196,24 @@ def time_device(torch, fn, steps, warmup, flush, world):
     barrier(torch, world)
     total = sum(s.elapsed_time(e) for s, e in ev)
     return max_over_ranks(torch, world, total)
+
+
+def time_device_streaming(torch, fn, steps, warmup, world):
+    """For kernels whose per-call working set exceeds L2 (no flush needed between calls):
+    `steps` back-to-back launches between one pair of CUDA events, so launch gaps do not count
+    against a ~30 us kernel. Returns the summed device milliseconds (max over ranks)."""
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        fn()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(torch, world)
+    s.record(stream)
+    for _ in range(steps):
+        fn()
+    e.record(stream)
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    return max_over_ranks(torch, world, s.elapsed_time(e))
 
 
 def cpu_baseline_gemm(a, b, a_sf, b_sf, scale, rows=256, budget_s=10.0):
@@ -349,10 +367,11 @@ def run_ours(args):
                                        y.data_ptr(), stream_h), "nvfp4_dequantize")
 
         for name, fn in (("quantize", quant_once), ("dequantize", dequant_once)):
-            t = time_device(torch, fn, args.steps, args.warmup, flush, world) / args.steps
+            t = time_device_streaming(torch, fn, args.steps, args.warmup, world) / args.steps
             gbs = QUANT_BYTES / (t * 1e-3) / 1e9
             line[name] = {"value": world * gbs, "unit": "GB/s", "ms_per_call": t,
                           "workload": "8192x8192 bf16, 0.5% x50 outliers, seed 1",
+                          "timing": "back-to-back launches, 164 MB touched per call (> 126 MB L2)",
                           "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_gbs,
                                        "unit": "GB/s", "frac": gbs / hbm_gbs,
                                        "traffic": profiled_traffic(f"{name}_8192"),

@@ -7,23 +7,28 @@
 // [rows, K/16]; fp32 accumulation; bf16 row-major output. The reference's SM120 warp-level
 // mma.sync design does not exist on sm_100a and is not followed. This kernel is:
 //
-//   * persistent: one CTA per SM walks output tiles of 128 x BN (BN = 256 or 128);
-//   * warp-specialised (320 threads):
+//   * persistent over output tiles, in two forms:
+//       single CTA (cta_group::1): 128 x 256 tiles, one CTA per SM (used when M <= 128);
+//       CTA pair  (cta_group::2, cluster of 2): 256 x 256 tiles; each CTA loads its own 128
+//               rows of A and its own 128-row half of B, the leader issues M=256 MMAs that read
+//               both CTAs' shared memory and accumulate into both CTAs' tensor memory; per-SM
+//               operand traffic per FLOP drops by a third and the ring is one stage deeper;
+//   * warp-specialised (320 threads per CTA):
 //       warp 8  TMA producer: A/B tiles (128B-swizzled) and scale-factor tiles into a
 //               STAGES-deep shared-memory ring, guarded by full and empty mbarriers;
 //       warps 0-3 scale-factor writers: read the API's row-major UE4M3 factors from shared
 //               memory and write them with tcgen05.st into the stage's tensor-memory slot, in
 //               the lane/column layout the block-scaled MMA reads (one warp per lane quarter);
-//       warp 9  MMA issuer: owns the tensor-memory allocation and issues tcgen05.mma
-//               .kind::mxf4nvf4.block_scale.scale_vec::4X (M=128, N=BN, K=64) into a TMEM fp32
-//               accumulator;
+//       warp 9  MMA issuer (the pair's leader only): owns the tensor-memory allocation and
+//               issues tcgen05.mma .kind::mxf4nvf4.block_scale.scale_vec::4X (K=64) into a
+//               TMEM fp32 accumulator;
 //       warps 4-7 epilogue: tcgen05.ld of the accumulator, x (1/scale), bf16 convert in
 //               registers, release of TMEM, then 64B-swizzled shared-memory staging and TMA
 //               tensor stores (bounds-clipped, so ragged M and N need no masking);
 //   * fault-safe: every mbarrier wait is bounded; a wait that times out raises a CTA-wide abort
 //     flag, every role returns, copies and MMAs in flight are drained (bounded), TMEM is freed,
 //     and NVFP4_ERR_DEVICE_TIMEOUT is recorded in the device status word.
-// No TMA load uses cluster multicast.
+// No TMA load uses cluster multicast: every CTA loads only into its own shared memory.
 #include <cstdint>
 #include <mutex>
 
@@ -36,7 +41,7 @@ __device__ int g_nvfp4_device_status = 0;
 namespace nvfp4 {
 namespace gemm {
 
-constexpr int kBM = 128;            // MMA M (one CTA, tcgen05 cta_group::1)
+constexpr int kRowsPerCta = 128;    // accumulator rows per CTA (TMEM lanes)
 constexpr int kBK = 256;            // K elements per pipeline stage = 128 packed bytes
 constexpr int kBKBytes = kBK / 2;
 constexpr int kUmmaK = 64;          // K per tcgen05.mma kind::mxf4nvf4
@@ -51,18 +56,23 @@ constexpr int kThreads = 32 * 10;
 constexpr int kEpiCols = 32;              // accumulator columns per epilogue store
 constexpr int kEpiBufBytes = 32 * kEpiCols * 2;  // 32 rows x 32 bf16 per epilogue warp
 
-template <int BN_, int STAGES_, int ACC_STAGES_>
+template <int BN_, int STAGES_, int ACC_STAGES_, bool PAIR_>
 struct Cfg {
   static constexpr int BN = BN_;
   static constexpr int STAGES = STAGES_;
   static constexpr int ACC_STAGES = ACC_STAGES_;
+  static constexpr bool PAIR = PAIR_;
+  static constexpr int CTAS = PAIR ? 2 : 1;
+  static constexpr int TILE_M = kRowsPerCta * CTAS;        // output rows per tile
+  static constexpr int B_ROWS = BN / CTAS;                 // B rows each CTA loads
   static_assert(BN % 128 == 0 && BN <= 256, "BN must be 128 or 256");
 
-  static constexpr int A_STAGE = kBM * kBKBytes;           // 16 KiB
-  static constexpr int B_STAGE = BN * kBKBytes;
-  static constexpr int SFA_STAGE = kBM * kSfBytesPerRow;   // 2 KiB
-  static constexpr int SFB_STAGE = BN * kSfBytesPerRow;
-  static constexpr uint32_t STAGE_TX = A_STAGE + B_STAGE + SFA_STAGE + SFB_STAGE;
+  static constexpr int A_STAGE = kRowsPerCta * kBKBytes;   // 16 KiB
+  static constexpr int B_STAGE = B_ROWS * kBKBytes;
+  static constexpr int SFA_STAGE = kRowsPerCta * kSfBytesPerRow;   // 2 KiB
+  static constexpr int SFB_STAGE = BN * kSfBytesPerRow;    // every CTA holds all BN rows
+  static constexpr uint32_t AB_TX = uint32_t(CTAS) * (A_STAGE + B_STAGE);  // pair total
+  static constexpr uint32_t SF_TX = SFA_STAGE + SFB_STAGE;                 // per CTA
 
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
@@ -70,7 +80,7 @@ struct Cfg {
   static constexpr int OFF_SFB = OFF_SFA + STAGES * SFA_STAGE;
   static constexpr int OFF_EPI = OFF_SFB + STAGES * SFB_STAGE;
   static constexpr int OFF_BAR = OFF_EPI + kNumEpiWarps * kEpiBufBytes;
-  static constexpr int NUM_BARS = 3 * STAGES + 2 * ACC_STAGES + 1;
+  static constexpr int NUM_BARS = 4 * STAGES + 2 * ACC_STAGES + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;     // slack to align the base to 1 KiB
@@ -79,9 +89,8 @@ struct Cfg {
   // Tensor memory columns: accumulators, then one scale-factor slot per pipeline stage, so the
   // factors of stage s+1 are written while the MMAs of stage s still read theirs. Within a slot:
   // B's factors for K-steps 0..3 (BN/32 columns each), then A's (4 columns each).
-  static constexpr uint32_t SFA_COLS_PER_STEP = 4;          // 128 rows -> one 32x4 chunk
-  static constexpr uint32_t SFB_COLS_PER_STEP = BN / 32;    // BN/128 chunks of 4 columns
-  static constexpr uint32_t SF_SLOT_COLS = kKSteps * (SFA_COLS_PER_STEP + SFB_COLS_PER_STEP);
+  static constexpr uint32_t SFB_COLS_PER_STEP = BN / 32;
+  static constexpr uint32_t SF_SLOT_COLS = kKSteps * (4 + SFB_COLS_PER_STEP);
   static constexpr uint32_t COL_SF = BN * ACC_STAGES;
   static constexpr uint32_t COLS_USED = COL_SF + STAGES * SF_SLOT_COLS;
   static constexpr uint32_t TMEM_COLS = COLS_USED <= 32 ? 32 : COLS_USED <= 64 ? 64
@@ -94,8 +103,8 @@ struct Params {
   float scale_val;
   int m;                   // rows of D
   int n;                   // columns of D
-  int m_blocks;
-  int n_blocks;
+  int m_blocks;            // tiles along M (TILE_M rows each)
+  int n_blocks;            // tiles along N (BN columns each)
   int k_stages;
   uint64_t timeout_ns;
 };
@@ -142,6 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
             const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
             const __grid_constant__ CUtensorMap tm_d, const Params p) {
+  constexpr bool kPair = C::PAIR;
+  constexpr int kGroup = C::CTAS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -151,28 +162,33 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   uint8_t* sSFB = smem + C::OFF_SFB;
   uint8_t* sEPI = smem + C::OFF_EPI;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* full_bar = bars;                                  // TMA -> scale-factor writers
-  uint64_t* sf_bar = bars + C::STAGES;                        // scale-factor writers -> MMA
-  uint64_t* empty_bar = bars + 2 * C::STAGES;                 // MMA (commit) -> TMA
-  uint64_t* tfull_bar = bars + 3 * C::STAGES;                 // MMA (commit) -> epilogue
-  uint64_t* tempty_bar = tfull_bar + C::ACC_STAGES;           // epilogue -> MMA
-  uint64_t* drain_bar = tempty_bar + C::ACC_STAGES;           // MMA drain before TMEM free
+  uint64_t* full_bar = bars;                        // A/B landed (leader's counts the pair)
+  uint64_t* sfload_bar = bars + C::STAGES;          // this CTA's scale-factor tiles landed
+  uint64_t* sf_bar = bars + 2 * C::STAGES;          // scale factors in TMEM (leader's, all CTAs)
+  uint64_t* empty_bar = bars + 3 * C::STAGES;       // MMA done with the stage -> producer
+  uint64_t* tfull_bar = bars + 4 * C::STAGES;       // accumulator ready -> epilogue
+  uint64_t* tempty_bar = tfull_bar + C::ACC_STAGES; // accumulator drained -> MMA (leader's)
+  uint64_t* drain_bar = tempty_bar + C::ACC_STAGES; // MMA drain before TMEM free
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = kPair ? ptx::cluster_ctarank() : 0u;
   const int num_tiles = p.m_blocks * p.n_blocks;
+  const int first_tile = kPair ? int(blockIdx.x >> 1) : int(blockIdx.x);
+  const int tile_step = kPair ? int(gridDim.x >> 1) : int(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
       ptx::mbar_init(&full_bar[i], 1);
-      ptx::mbar_init(&sf_bar[i], kNumSfWarps);
+      ptx::mbar_init(&sfload_bar[i], 1);
+      ptx::mbar_init(&sf_bar[i], kNumSfWarps * C::CTAS);
       ptx::mbar_init(&empty_bar[i], 1);
     }
     for (int i = 0; i < C::ACC_STAGES; ++i) {
       ptx::mbar_init(&tfull_bar[i], 1);
-      ptx::mbar_init(&tempty_bar[i], kNumEpiWarps);
+      ptx::mbar_init(&tempty_bar[i], kNumEpiWarps * C::CTAS);
     }
     ptx::mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -186,11 +202,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     ptx::tma_prefetch_desc(&tm_d);
   }
   if (warp == kMmaWarp) {
-    ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
-    ptx::tmem_relinquish_alloc_permit();
+    ptx::tmem_alloc_g<kGroup>(tmem_slot, C::TMEM_COLS);
+    ptx::tmem_relinquish_g<kGroup>();
   }
   ptx::tc_fence_before_sync();
-  __syncthreads();
+  if constexpr (kPair) ptx::cluster_sync(); else __syncthreads();
   ptx::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -200,48 +216,66 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       int stage = 0;
       uint32_t phase = 0;
       int64_t fills = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile % p.m_blocks) * kBM;
+      for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+        const int m_cta = (tile % p.m_blocks) * C::TILE_M + int(rank) * kRowsPerCta;
         const int n0 = (tile / p.m_blocks) * C::BN;
+        const int n_cta = n0 + int(rank) * C::B_ROWS;
         for (int kb = 0; kb < p.k_stages; ++kb) {
-          if (!ptx::mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.timeout_ns)) goto producer_done;
-          ptx::mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_TX);
-          ptx::tma_load_2d(sA + stage * C::A_STAGE, &tm_a, &full_bar[stage], kb * kBKBytes, m0);
-          ptx::tma_load_2d(sB + stage * C::B_STAGE, &tm_b, &full_bar[stage], kb * kBKBytes, n0);
-          ptx::tma_load_2d(sSFA + stage * C::SFA_STAGE, &tm_sfa, &full_bar[stage], kb * kSfBytesPerRow, m0);
-          ptx::tma_load_2d(sSFB + stage * C::SFB_STAGE, &tm_sfb, &full_bar[stage], kb * kSfBytesPerRow, n0);
+          if (!ptx::mbar_wait<kPair>(&empty_bar[stage], phase ^ 1, abort_flag, p.timeout_ns))
+            goto producer_done;
+          if (rank == 0) ptx::mbar_arrive_expect_tx(&full_bar[stage], C::AB_TX);
+          if constexpr (kPair) {
+            ptx::tma_load_2d_pair(sA + stage * C::A_STAGE, &tm_a, &full_bar[stage], kb * kBKBytes, m_cta);
+            ptx::tma_load_2d_pair(sB + stage * C::B_STAGE, &tm_b, &full_bar[stage], kb * kBKBytes, n_cta);
+          } else {
+            ptx::tma_load_2d(sA + stage * C::A_STAGE, &tm_a, &full_bar[stage], kb * kBKBytes, m_cta);
+            ptx::tma_load_2d(sB + stage * C::B_STAGE, &tm_b, &full_bar[stage], kb * kBKBytes, n_cta);
+          }
+          ptx::mbar_arrive_expect_tx(&sfload_bar[stage], C::SF_TX);
+          ptx::tma_load_2d(sSFA + stage * C::SFA_STAGE, &tm_sfa, &sfload_bar[stage], kb * kSfBytesPerRow, m_cta);
+          ptx::tma_load_2d(sSFB + stage * C::SFB_STAGE, &tm_sfb, &sfload_bar[stage], kb * kSfBytesPerRow, n0);
           ++fills;
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
         }
       }
     producer_done:
       // Never leave a TMA write in flight into shared memory of an exiting CTA: wait (bounded,
-      // ignoring the abort flag) until the most recent fill of every slot has landed.
+      // ignoring the abort flag) until the most recent fill of every slot has landed. In a pair
+      // the A/B bytes of both CTAs are counted on the leader's barriers; the follower waits a
+      // fixed bounded time after an abort instead.
       {
         int no_abort = 0;
         const int64_t last = fills < C::STAGES ? fills : C::STAGES;
         for (int64_t i = 0; i < last; ++i) {
           const int64_t f = fills - 1 - i;
-          ptx::mbar_wait(&full_bar[f % C::STAGES], uint32_t((f / C::STAGES) & 1), &no_abort,
-                         p.timeout_ns);
+          const uint32_t par = uint32_t((f / C::STAGES) & 1);
+          ptx::mbar_wait<kPair>(&sfload_bar[f % C::STAGES], par, &no_abort, p.timeout_ns);
+          if (rank == 0)
+            ptx::mbar_wait<kPair>(&full_bar[f % C::STAGES], par, &no_abort, p.timeout_ns);
+        }
+        if (kPair && rank != 0 && *abort_flag) {
+          const uint64_t t0 = ptx::globaltimer_ns();
+          while (ptx::globaltimer_ns() - t0 < 1000000ull) {
+          }
         }
       }
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = ptx::make_idesc_mxf4nvf4(kBM, C::BN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = ptx::make_idesc_mxf4nvf4(C::TILE_M, C::BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        if (!ptx::mbar_wait(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.timeout_ns)) goto mma_done;
+      for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+        if (!ptx::mbar_wait<kPair>(&tempty_bar[acc], acc_phase ^ 1, abort_flag, p.timeout_ns))
+          goto mma_done;
         ptx::tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * C::BN);
         for (int kb = 0; kb < p.k_stages; ++kb) {
-          if (!ptx::mbar_wait(&sf_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
-          if (!ptx::mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
+          if (!ptx::mbar_wait<kPair>(&sf_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
+          if (!ptx::mbar_wait<kPair>(&full_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
           ptx::tc_fence_after_sync();
           const uint32_t t_sfb = tmem_base + C::COL_SF + uint32_t(stage) * C::SF_SLOT_COLS;
           const uint32_t t_sfa = t_sfb + C::BN / 8;
@@ -252,34 +286,42 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
             // K-step j starts 32 bytes further along the 128-byte swizzled rows.
             const uint64_t a_desc = ptx::make_smem_desc(a_s + j * 32, 0, 1024, ptx::kLayoutSW128);
             const uint64_t b_desc = ptx::make_smem_desc(b_s + j * 32, 0, 1024, ptx::kLayoutSW128);
-            ptx::tc_mma_mxf4nvf4(d_tmem, a_desc, b_desc, idesc, t_sfa + 4 * j,
-                                 t_sfb + j * (C::BN / 32), (kb | j) != 0 ? 1u : 0u);
+            if constexpr (kPair)
+              ptx::tc_mma_mxf4nvf4_pair(d_tmem, a_desc, b_desc, idesc, t_sfa + 4 * j,
+                                        t_sfb + j * (C::BN / 32), (kb | j) != 0 ? 1u : 0u);
+            else
+              ptx::tc_mma_mxf4nvf4(d_tmem, a_desc, b_desc, idesc, t_sfa + 4 * j,
+                                   t_sfb + j * (C::BN / 32), (kb | j) != 0 ? 1u : 0u);
           }
-          ptx::tc_commit(&empty_bar[stage]);  // frees the smem slot and its TMEM scale slot
+          // frees the stage's smem and TMEM scale slot (in both CTAs of a pair)
+          if constexpr (kPair) ptx::tc_commit_pair(&empty_bar[stage], 0x3);
+          else ptx::tc_commit(&empty_bar[stage]);
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
         }
-        ptx::tc_commit(&tfull_bar[acc]);      // accumulator ready for the epilogue
+        if constexpr (kPair) ptx::tc_commit_pair(&tfull_bar[acc], 0x3);
+        else ptx::tc_commit(&tfull_bar[acc]);
         if (++acc == C::ACC_STAGES) { acc = 0; acc_phase ^= 1; }
       }
     mma_done:
       // Drain every tcgen05 operation this thread issued before TMEM is released.
       {
         int no_abort = 0;
-        ptx::tc_commit(drain_bar);
-        ptx::mbar_wait(drain_bar, 0, &no_abort, p.timeout_ns);
+        if constexpr (kPair) ptx::tc_commit_pair(drain_bar, 0x1);
+        else ptx::tc_commit(drain_bar);
+        ptx::mbar_wait<kPair>(drain_bar, 0, &no_abort, p.timeout_ns);
       }
     }
   } else if (warp < kNumSfWarps) {
     // ------------------------------------------------------------------ scale-factor writers
-    // Stage s's TMEM slot is rewritten only after full[s] of its next fill, which the producer
-    // issues after empty[s]: the MMAs that read the slot's previous contents have completed.
+    // Stage s's TMEM slot is rewritten only after sfload[s] of its next fill, which the
+    // producer issues after empty[s]: the MMAs that read the slot's previous contents are done.
     const int q = warp;
     const uint32_t lane_base = uint32_t(q * 32) << 16;
     int stage = 0;
     uint32_t phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
       for (int kb = 0; kb < p.k_stages; ++kb) {
-        const bool ok = ptx::mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns);
+        const bool ok = ptx::mbar_wait<kPair>(&sfload_bar[stage], phase, abort_flag, p.timeout_ns);
         if (!__all_sync(0xFFFFFFFFu, ok)) goto sf_done;
         write_sf_slot<C>(tmem_base + lane_base + C::COL_SF + uint32_t(stage) * C::SF_SLOT_COLS,
                          ptx::smem_u32(sSFA + stage * C::SFA_STAGE),
@@ -287,7 +329,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         ptx::tmem_wait_st();
         ptx::tc_fence_before_sync();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&sf_bar[stage]);
+        if (lane == 0) {
+          if constexpr (kPair) ptx::mbar_arrive_cta(&sf_bar[stage], 0);
+          else ptx::mbar_arrive(&sf_bar[stage]);
+        }
         if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
       }
     }
@@ -302,10 +347,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     const uint32_t swz = uint32_t((lane >> 1) & 3);  // 64-byte TMA swizzle of row `lane`
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int m0 = (tile % p.m_blocks) * kBM;
+    for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+      const int m_cta = (tile % p.m_blocks) * C::TILE_M + int(rank) * kRowsPerCta;
       const int n0 = (tile / p.m_blocks) * C::BN;
-      const bool ok = ptx::mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, p.timeout_ns);
+      const bool ok = ptx::mbar_wait<kPair>(&tfull_bar[acc], acc_phase, abort_flag, p.timeout_ns);
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
       ptx::tc_fence_after_sync();
       const uint32_t t_row = tmem_base + (uint32_t(ew * 32) << 16) + uint32_t(acc * C::BN);
@@ -329,7 +374,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       }
       ptx::tc_fence_before_sync();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+      if (lane == 0) {
+        if constexpr (kPair) ptx::mbar_arrive_cta(&tempty_bar[acc], 0);
+        else ptx::mbar_arrive(&tempty_bar[acc]);
+      }
 #pragma unroll
       for (int c = 0; c < C::BN / kEpiCols; ++c) {
         if (lane == 0) ptx::bulk_wait_group_read<0>();  // previous store has read the buffer
@@ -344,8 +392,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         __syncwarp();
         // Boxes that start inside D are clipped by the TMA unit; boxes entirely outside
         // (ragged M or N) are skipped.
-        if (lane == 0 && m0 + ew * 32 < p.m && n0 + c * kEpiCols < p.n) {
-          ptx::tma_store_2d(&tm_d, buf, n0 + c * kEpiCols, m0 + ew * 32);
+        if (lane == 0 && m_cta + ew * 32 < p.m && n0 + c * kEpiCols < p.n) {
+          ptx::tma_store_2d(&tm_d, buf, n0 + c * kEpiCols, m_cta + ew * 32);
           ptx::bulk_commit_group();
         }
       }
@@ -355,12 +403,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   }
 
   ptx::tc_fence_before_sync();
-  __syncthreads();
+  if constexpr (kPair) ptx::cluster_sync(); else __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) atomicCAS(&g_nvfp4_device_status, 0, NVFP4_ERR_DEVICE_TIMEOUT);
   if (warp == kMmaWarp) {
     __syncwarp();
     ptx::tc_fence_after_sync();
-    ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
+    ptx::tmem_dealloc_g<kGroup>(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -426,39 +474,64 @@ bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint6
 
 constexpr int kMaxDevices = 64;
 
+// Per device, once: raise the dynamic shared-memory limit and find how many CTAs (single) or
+// CTA pairs (clusters of 2) can be resident at once — the persistent grid size.
 template <class C>
-int set_smem_attr_once(int dev) {
+int resident_units(int dev) {
   static std::once_flag flags[kMaxDevices];
+  static int units[kMaxDevices];
   static cudaError_t errs[kMaxDevices];
-  if (dev < 0 || dev >= kMaxDevices) return NVFP4_ERR_NO_DEVICE;
+  if (dev < 0 || dev >= kMaxDevices) return -NVFP4_ERR_NO_DEVICE;
   std::call_once(flags[dev], [&] {
     errs[dev] = cudaFuncSetAttribute(gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::SMEM_ALLOC);
+    if (errs[dev] != cudaSuccess) return;
+    int sms = 0;
+    errs[dev] = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (errs[dev] != cudaSuccess) return;
+    if constexpr (C::PAIR) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(sms & ~1);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = C::SMEM_ALLOC;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      errs[dev] = cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<C>, &cfg);
+      units[dev] = clusters > 0 ? clusters : sms / 2;
+    } else {
+      units[dev] = sms;
+    }
   });
-  return status_from_cuda(errs[dev]);
+  if (errs[dev] != cudaSuccess) return -NVFP4_ERR_CUDA;
+  return units[dev];
 }
 
-using CfgWide = Cfg<256, 4, 1>;    // 128 x 256 tiles, 4-stage ring, one accumulator
-using CfgNarrow = Cfg<128, 6, 2>;  // 128 x 128 tiles, 6-stage ring, double-buffered accumulator
+using CfgSingle = Cfg<256, 4, 1, false>;  // 128 x 256 tiles, one CTA, 4-stage ring
+using CfgPair = Cfg<256, 5, 1, true>;     // 256 x 256 tiles, CTA pair, 5-stage ring per CTA
 
 template <class C>
 int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
            const float* scale_ptr, float scale_val, void* D, int64_t M, int64_t N, int64_t K,
            cudaStream_t stream) {
   int dev = 0;
-  const int sms = current_device_sm_count(&dev);
-  if (sms <= 0) return NVFP4_ERR_NO_DEVICE;
-  int st = set_smem_attr_once<C>(dev);
-  if (st != NVFP4_OK) return st;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NVFP4_ERR_NO_DEVICE;
+  const int units = resident_units<C>(dev);
+  if (units <= 0) return units == 0 ? NVFP4_ERR_NO_DEVICE : -units;
 
   CUtensorMap tm_a, tm_b, tm_sfa, tm_sfb, tm_d;
   const uint64_t kb = uint64_t(K) / 2, ks = uint64_t(K) / 16;
-  bool ok = make_map_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, kb, M, kb, kBKBytes, kBM,
+  bool ok = make_map_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, kb, M, kb, kBKBytes, kRowsPerCta,
                         CU_TENSOR_MAP_SWIZZLE_128B) &&
-            make_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, B, kb, N, kb, kBKBytes, C::BN,
+            make_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, B, kb, N, kb, kBKBytes, C::B_ROWS,
                         CU_TENSOR_MAP_SWIZZLE_128B) &&
             make_map_2d(&tm_sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, A_sf, ks, M, ks, kSfBytesPerRow,
-                        kBM, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                        kRowsPerCta, CU_TENSOR_MAP_SWIZZLE_NONE) &&
             make_map_2d(&tm_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, B_sf, ks, N, ks, kSfBytesPerRow,
                         C::BN, CU_TENSOR_MAP_SWIZZLE_NONE) &&
             make_map_2d(&tm_d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, D, N, M, uint64_t(N) * 2,
@@ -470,14 +543,32 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
   p.scale_val = scale_val;
   p.m = int(M);
   p.n = int(N);
-  p.m_blocks = int((M + kBM - 1) / kBM);
+  p.m_blocks = int((M + C::TILE_M - 1) / C::TILE_M);
   p.n_blocks = int((N + C::BN - 1) / C::BN);
   p.k_stages = int(K / kBK);
   p.timeout_ns = 2000000000ull;  // 2 s per wait: far above any legitimate stall
   const int64_t tiles = int64_t(p.m_blocks) * p.n_blocks;
-  const int grid = int(tiles < sms ? tiles : sms);
-  gemm_kernel<C><<<grid, kThreads, C::SMEM_ALLOC, stream>>>(tm_a, tm_b, tm_sfa, tm_sfb, tm_d, p);
-  return status_from_cuda(cudaGetLastError());
+  const int grid_units = int(tiles < units ? tiles : units);
+  if constexpr (C::PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * grid_units);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM_ALLOC;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return status_from_cuda(cudaLaunchKernelEx(&cfg, gemm_kernel<C>, tm_a, tm_b, tm_sfa, tm_sfb,
+                                               tm_d, p));
+  } else {
+    gemm_kernel<C><<<grid_units, kThreads, C::SMEM_ALLOC, stream>>>(tm_a, tm_b, tm_sfa, tm_sfb,
+                                                                   tm_d, p);
+    return status_from_cuda(cudaGetLastError());
+  }
 }
 
 int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const float* scale_ptr,
@@ -496,7 +587,10 @@ int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const 
   if (!A || !B || !A_sf || !B_sf) return NVFP4_ERR_INVALID_VALUE;
   if (!aligned_to(A, 16) || !aligned_to(B, 16) || !aligned_to(A_sf, 16) || !aligned_to(B_sf, 16))
     return NVFP4_ERR_MISALIGNED;
-  return launch<CfgWide>(A, B, A_sf, B_sf, scale_ptr, scale_val, D, M, N, K, stream);
+  // A CTA pair covers 256 rows; for M <= 128 a single CTA per tile wastes no tensor work.
+  if (M > kRowsPerCta)
+    return launch<CfgPair>(A, B, A_sf, B_sf, scale_ptr, scale_val, D, M, N, K, stream);
+  return launch<CfgSingle>(A, B, A_sf, B_sf, scale_ptr, scale_val, D, M, N, K, stream);
 }
 
 }  // namespace gemm

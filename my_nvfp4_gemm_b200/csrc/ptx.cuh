@@ -156,16 +156,61 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Same, with cluster-scope acquire: for barriers that threads of the peer CTA arrive on.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Rank of this CTA in its cluster, and the shared::cluster address of `local`'s counterpart in
+// CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_cta(const void* local, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
+  return out;
+}
+// Arrive on the barrier at `local`'s offset in CTA `rank` of the cluster (default semantics).
+// Callers order their tensor-memory writes/reads before it with tcgen05.wait::{st,ld} and
+// tcgen05.fence::before_thread_sync. (An explicit .release.cluster arrive measured ~0.7 us per
+// call here, enough to throttle a per-stage handshake; the default form costs ~30 ns.)
+__device__ __forceinline__ void mbar_arrive_cta(uint64_t* local, uint32_t rank) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(map_to_cta(local, rank))
+               : "memory");
+}
+// All threads of all CTAs in the cluster.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
 // Bounded wait on the phase with the given parity. Returns true once the phase completed.
 // Returns false if `*abort` becomes non-zero (another role gave up) or if `timeout_ns`
 // elapses; in the latter case it raises `*abort` itself so the CTA's other roles stop too.
+template <bool kClusterScope = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto try_once = [&]() {
+    return kClusterScope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+  };
+  if (try_once()) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (try_once()) return true;
     if ((++n & 63u) == 0u) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > timeout_ns) {
@@ -190,6 +235,17 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// CTA-pair form: the data lands in this CTA's shared memory, the transaction bytes are
+// counted on the barrier at `bar`'s offset in the pair's leader CTA (rank 0). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map,
+                                                 uint64_t* bar, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(map_to_cta(bar, 0)), "r"(x), "r"(y)
       : "memory");
 }
 
@@ -232,6 +288,30 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
 }
+template <int kCtaGroup>
+__device__ __forceinline__ void tmem_alloc_g(uint32_t* smem_result, uint32_t ncols) {
+  if constexpr (kCtaGroup == 1)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(smem_result)), "r"(ncols) : "memory");
+  else
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(smem_result)), "r"(ncols) : "memory");
+}
+template <int kCtaGroup>
+__device__ __forceinline__ void tmem_relinquish_g() {
+  if constexpr (kCtaGroup == 1)
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  else
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+template <int kCtaGroup>
+__device__ __forceinline__ void tmem_dealloc_g(uint32_t taddr, uint32_t ncols) {
+  if constexpr (kCtaGroup == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+  else
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before_sync() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -244,6 +324,15 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           smem_u32(bar))
+      : "memory");
+}
+
+// CTA-pair commit: arrive once on the barrier at `bar`'s offset in every CTA of `cta_mask`
+// when the pair's MMAs issued so far have completed (a completion signal, not a data load).
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)), "h"(cta_mask)
       : "memory");
 }
 
@@ -288,6 +377,23 @@ __device__ __forceinline__ void tc_mma_mxf4nvf4(uint32_t d_tmem, uint64_t a_desc
       ".reg .pred p;\n"
       "setp.ne.b32 p, %4, 0;\n"
       "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X"
+      " [%0], %1, %2, %3, [%5], [%6], p;\n"
+      "}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// CTA-pair form, issued by the leader: M = 256 rows split across the pair's TMEMs; A from each
+// CTA's own shared memory, B's N/2-row halves from each CTA's shared memory.
+__device__ __forceinline__ void tc_mma_mxf4nvf4_pair(uint32_t d_tmem, uint64_t a_desc,
+                                                     uint64_t b_desc, uint32_t idesc,
+                                                     uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X"
       " [%0], %1, %2, %3, [%5], [%6], p;\n"
       "}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)

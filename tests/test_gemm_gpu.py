@@ -104,14 +104,19 @@ def test_gemm_host_scale_matches_device_scale(oracle):
     assert np.array_equal(capi_gemm(A, B, Asf, Bsf, 0.75, True), capi_gemm(A, B, Asf, Bsf, 0.75, False))
 
 
-def test_gemm_single_nonzero_scale_factor_positions(oracle):
+@pytest.mark.parametrize("M", [128, 256])
+def test_gemm_single_nonzero_scale_factor_positions(oracle, M):
     """Isolates the scale-factor TMEM layout: one non-unit scale factor at a time, in every
-    32-row quarter of the A tile, both 128-row halves of the B tile and every K step."""
-    M, N, K = 128, 256, 512
+    32-row quarter of the A tile (both CTAs of a pair at M=256), both 128-row halves of the
+    B tile and every K step."""
+    N, K = 256, 512
     rng = np.random.default_rng(11)
     A, B, _, _ = random_operands(rng, M, N, K)
     one = 0x38  # 1.0
-    for (r, n, kb) in [(0, 0, 0), (37, 5, 3), (70, 131, 9), (127, 255, 31), (96, 200, 16)]:
+    rows = [(0, 0, 0), (37, 5, 3), (70, 131, 9), (127, 255, 31), (96, 200, 16)]
+    if M == 256:
+        rows += [(128, 3, 2), (165, 140, 7), (255, 255, 30), (200, 77, 12)]
+    for (r, n, kb) in rows:
         Asf = np.full((M, K // 16), one, np.uint8)
         Bsf = np.full((N, K // 16), one, np.uint8)
         Asf[r, kb] = 0x48  # 4.0
