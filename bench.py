@@ -49,6 +49,12 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-quant", action="store_true")
     ap.add_argument("--size", type=int, default=8192, help="M = N = K (profiling of small cases)")
+    ap.add_argument("--workload", choices=["square", "decode", "prefill"], default="square",
+                    help="square: 8192^3 (headline); decode: M x 28672 x 8192; "
+                         "prefill: 16384 x 57344 x 8192 (N sharded across ranks)")
+    ap.add_argument("--m", type=int, default=128, help="decode tokens (16, 32, 64, 128)")
+    ap.add_argument("--gather", action="store_true",
+                    help="prefill/decode: include the chunked NCCL all-gather of D in the timing")
     return ap.parse_args()
 
 
@@ -265,13 +271,14 @@ def run_reference_arm(args):
     Bb = cases.activation(rng, size, size)
     sA, sB = O.global_scale(Ab), O.global_scale(Bb)
 
+    qa, fa = O.quantize(Ab, sA)            # operands quantized once, as on the GPU arm
+    qb, fb = O.quantize(Bb, sB)
+    scale = torch.tensor(np.float32(sA) * np.float32(sB))
+
     def step():
-        qa, fa = O.quantize(Ab, sA)        # activation quantize (the sample's rows)
-        qb, fb = O.quantize(Bb, sB)
         da = torch.from_numpy(O.decode_scaled(qa, fa))
         db = torch.from_numpy(O.decode_scaled(qb, fb))
-        d = ((da @ db.T) / torch.tensor(np.float32(sA) * np.float32(sB))).to(torch.bfloat16)
-        return d
+        return ((da @ db.T) / scale).to(torch.bfloat16)
 
     for _ in range(max(args.warmup, 1)):
         step()
@@ -282,8 +289,9 @@ def run_reference_arm(args):
     flops = 2.0 * rows * size * size
     val = flops / dt / 1e12
     cores = torch.get_num_threads()
-    sample = (f"{rows} of {size} rows of A x full B ({size}x{size}), per step: quantize A-rows and "
-              f"B (oracle, OpenMP {O.num_threads()} threads) + decode + torch fp32 matmul + bf16")
+    sample = (f"{rows} of {size} rows of A x full B ({size}x{size}) per step: decode of the "
+              f"block-scaled operands (oracle, OpenMP {O.num_threads()} threads) + torch fp32 "
+              f"matmul + / scale + bf16")
     line = {"metric": "nvfp4_gemm_tflops", "value": val, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/ue4m3->f32",
@@ -423,10 +431,94 @@ def run_ours(args):
     return 0
 
 
+def run_sharded_workload(args):
+    """decode / prefill: a fixed global problem (strong scaling) whose weight is sharded
+    column-parallel across the ranks; A is replicated. Optionally times the chunked NCCL
+    all-gather of D together with the GEMM."""
+    import torch
+    from my_nvfp4_gemm_b200 import capi, load_my_plugins, sharded
+    plugins = load_my_plugins()
+    world, rank, local = dist_setup(torch)
+    K = 8192
+    if args.workload == "decode":
+        M, N, seed, frac, name = args.m, 28672, 3, 0.0, f"decode_m{args.m}_n28672_k8192"
+    else:
+        M, N, seed, frac, name = 16384, 57344, 4, 0.005, "prefill_16384x57344x8192"
+    n0, n1 = sharded.shard_range(N, world, rank)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    X = torch.randn(M, K, device="cuda", generator=g)
+    if frac:
+        idx = torch.randperm(X.numel(), device="cuda", generator=g)[: int(frac * X.numel())]
+        X.view(-1)[idx] *= 50.0
+    X = X.to(torch.bfloat16)
+    sX = (6 * 448 / X.abs().max().to(torch.float32)).reshape(())
+    x, x_sf = plugins.quantize_nvfp4(X, sX)
+    del X
+    # the weight: quantized shard by shard (N(0, 0.02^2)), global scale over the whole weight
+    gw = torch.Generator(device="cuda").manual_seed(seed + 1000)
+    W = (torch.randn(N, K, device="cuda", generator=gw) * 0.02).to(torch.bfloat16)
+    sW = (6 * 448 / W.abs().max().to(torch.float32)).reshape(())
+    w, w_sf = plugins.quantize_nvfp4(W[n0:n1].contiguous(), sW)
+    del W
+    torch.cuda.empty_cache()
+    scale = (sX * sW).reshape(())
+    n_loc = n1 - n0
+    d = torch.empty(M, n_loc, dtype=torch.bfloat16, device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    stream_h = torch.cuda.current_stream().cuda_stream
+    ptrs = (x.data_ptr(), w.data_ptr(), x_sf.data_ptr(), w_sf.data_ptr(), scale.data_ptr(), d.data_ptr())
+
+    if args.gather and world > 1:
+        def step():
+            sharded.gemm_column_parallel(x, w, x_sf, w_sf, scale, gather=True, chunks=4)
+    else:
+        def step():
+            st = capi.gemm(*ptrs, M, n_loc, K, stream_h)
+            if st:
+                raise capi.NvFp4Error(st, "nvfp4_gemm")
+
+    hbm_gbs, bf16_tf, peak_src = measured_peaks()
+    sampler = ClockSampler(gpu_uuid(torch, torch.cuda.current_device()))
+    with sampler:
+        total = time_device(torch, step, args.steps, args.warmup, flush, world)
+    ms = total / args.steps
+    flops = 2.0 * M * N * K
+    # algorithmic bytes of this rank's GEMM: its weight shard + scales, the activation, D shard
+    bytes_rank = n_loc * K * (0.5 + 1 / 16) + M * K * (0.5 + 1 / 16) + 2.0 * M * n_loc
+    achieved_tf = 2.0 * M * n_loc * K / (ms * 1e-3) / 1e12
+    achieved_gbs = bytes_rank / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "nvfp4_gemm_tflops", "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "e2m1/ue4m3->f32", "data": "synthetic",
+        "config": {"workload": name, "M": M, "N": N, "K": K, "n_per_rank": n_loc,
+                   "parallelism": f"column-parallel N x{world}",
+                   "all_gather_in_timing": bool(args.gather and world > 1),
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "roofline": {"bound": "hbm" if M <= 128 else "tensor",
+                     "achieved_tflops": achieved_tf, "frac_fp4_peak": achieved_tf / (4 * bf16_tf),
+                     "achieved_gbs": achieved_gbs, "frac_hbm": achieved_gbs / hbm_gbs,
+                     "algorithmic_bytes_per_rank": bytes_rank,
+                     "peak_source": f"{peak_src}: HBM {hbm_gbs} GB/s, FP4 4 x bf16 {bf16_tf} TF/s"},
+        "gpu_launches": args.steps * (4 if (args.gather and world > 1) else 1),
+        "clocks": sampler.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.workload != "square":
+        return run_sharded_workload(args)
     return run_ours(args)
 
 

@@ -178,11 +178,26 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
+__device__ __forceinline__ uint32_t map_addr_to_cta(uint32_t smem_addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr), "r"(rank));
+  return out;
+}
 __device__ __forceinline__ uint32_t map_to_cta(const void* local, uint32_t rank) {
   uint32_t out;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
   return out;
 }
+// 16-byte load from another CTA's shared memory (distributed shared memory) at a
+// shared::cluster address obtained with map_to_cta().
+__device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t cluster_addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(cluster_addr));
+  return v;
+}
+
 // Arrive on the barrier at `local`'s offset in CTA `rank` of the cluster (default semantics).
 // Callers order their tensor-memory writes/reads before it with tcgen05.wait::{st,ld} and
 // tcgen05.fence::before_thread_sync. (An explicit .release.cluster arrive measured ~0.7 us per
