@@ -64,6 +64,21 @@ int nvfp4_quantize_host_scale(const void* input, float input_scale, int64_t nume
                               void* output, void* output_sf, cudaStream_t stream);
 
 /*
+ * Quantize with the per-tensor scale computed on the device, in one call and with no host
+ * synchronisation: amax = NaN-propagating max |x|, s = fp32(1/amax) * 2688 — exactly how torch
+ * evaluates the reference recipe `6*448 / A.abs().max().float()` (test.py:10-11) — then the
+ * quantization of nvfp4_quantize with that s. *scale_out (device fp32) receives s.
+ * `workspace` is a device buffer of at least nvfp4_quantize_auto_scale_workspace_bytes(numel)
+ * bytes (4-byte aligned) that the call uses for partial maxima; its contents on entry do not
+ * matter. Same input/output rules as nvfp4_quantize. No reference counterpart (the reference
+ * computes the scale in torch and synchronises the host with .item()).
+ */
+int64_t nvfp4_quantize_auto_scale_workspace_bytes(int64_t numel);
+int nvfp4_quantize_auto_scale(const void* input, int64_t numel, void* output, void* output_sf,
+                              float* scale_out, void* workspace, int64_t workspace_bytes,
+                              cudaStream_t stream);
+
+/*
  * Dequantize NVFP4 -> bf16.
  * Replaces my_plugins::de_quantize_nvfp4 (csrc/quantize/quantize_nvfp4.h:7, launcher
  * csrc/quantize/quantize_nvfp4.cu:64-68). `n_bytes` is the packed byte count, as in the

@@ -34,6 +34,8 @@ SIGNATURES = {
     "nvfp4_version": ([], _INT),
     "nvfp4_quantize": ([_P, _P, _I64, _P, _P, _P], _INT),
     "nvfp4_quantize_host_scale": ([_P, _F32, _I64, _P, _P, _P], _INT),
+    "nvfp4_quantize_auto_scale_workspace_bytes": ([_I64], _I64),
+    "nvfp4_quantize_auto_scale": ([_P, _I64, _P, _P, _P, _P, _I64, _P], _INT),
     "nvfp4_dequantize": ([_P, _P, _P, _I64, _P, _P], _INT),
     "nvfp4_dequantize_host_scale": ([_P, _F32, _P, _I64, _P, _P], _INT),
     "nvfp4_gemm": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P], _INT),
@@ -84,6 +86,16 @@ def quantize(x_ptr, scale_ptr, numel, out_ptr, sf_ptr, stream=0) -> int:
 
 def quantize_host_scale(x_ptr, scale, numel, out_ptr, sf_ptr, stream=0) -> int:
     return lib().nvfp4_quantize_host_scale(x_ptr, scale, numel, out_ptr, sf_ptr, stream)
+
+
+def quantize_auto_scale_workspace_bytes(numel) -> int:
+    return int(lib().nvfp4_quantize_auto_scale_workspace_bytes(numel))
+
+
+def quantize_auto_scale(x_ptr, numel, out_ptr, sf_ptr, scale_out_ptr, ws_ptr, ws_bytes,
+                        stream=0) -> int:
+    return lib().nvfp4_quantize_auto_scale(x_ptr, numel, out_ptr, sf_ptr, scale_out_ptr, ws_ptr,
+                                           ws_bytes, stream)
 
 
 def dequantize(q_ptr, scale_ptr, sf_ptr, n_bytes, out_ptr, stream=0) -> int:

@@ -42,13 +42,16 @@ __device__ __forceinline__ uint32_t max_bf16x2(uint32_t acc, uint32_t w) {
 }
 
 // One thread = one half-block of 8 bf16. Lanes 2j and 2j+1 hold the two halves of a block.
-template <bool kDeviceScale>
+// kReverse: CTA b processes the chunk of CTA (grid-1-b). Used after a forward pass over the same
+// input (the amax pass), whose most recently read chunks are still resident in L2.
+template <bool kDeviceScale, bool kReverse = false>
 __global__ void __launch_bounds__(kThreads)
 quantize_kernel(const uint4* __restrict__ x, const float* __restrict__ scale_ptr, float scale_val,
                 int64_t n_half_blocks, uint32_t* __restrict__ q, uint8_t* __restrict__ sf) {
-  const float s = kDeviceScale ? __ldg(scale_ptr) : scale_val;
+  const float s = kDeviceScale ? *scale_ptr : scale_val;
   const float rcp_s = __frcp_rn(s);
-  const int64_t base = int64_t(blockIdx.x) * kHalfBlocksPerCta + threadIdx.x;
+  const int64_t cta = kReverse ? int64_t(gridDim.x - 1 - blockIdx.x) : int64_t(blockIdx.x);
+  const int64_t base = cta * kHalfBlocksPerCta + threadIdx.x;
 
   uint4 v[kUnroll];
 #pragma unroll
@@ -121,6 +124,63 @@ dequantize_kernel(const uint32_t* __restrict__ q, const float* __restrict__ scal
   }
 }
 
+// ---- per-tensor scale on the device -----------------------------------------------------
+// The reference recipe (test.py:10-11) is evaluated by torch as
+//   amax = bf16 max|x| (NaN-propagating), s = fp32(1 / fp32(amax)) * 2688.
+// For bf16 magnitudes the 15-bit pattern (bits & 0x7FFF) orders like the value, and every NaN
+// pattern is above +inf, so an unsigned integer max over magnitude bits is exactly that max,
+// NaN included.
+constexpr int64_t kAmaxChunk = 131072;            // bf16 elements reduced by one CTA
+constexpr int kAmaxThreads = 512;
+
+__device__ __forceinline__ uint32_t mag_max_bf16x2(uint32_t m, uint32_t w) {
+  return max(m, max(w & 0x7FFFu, (w >> 16) & 0x7FFFu));
+}
+
+// One partial (magnitude bits of the chunk's max |x|) per kAmaxChunk elements.
+__global__ void __launch_bounds__(kAmaxThreads)
+amax_partial_kernel(const uint4* __restrict__ x, int64_t n_vec, uint32_t* __restrict__ partial) {
+  const int64_t v0 = int64_t(blockIdx.x) * (kAmaxChunk / 8);
+  const int64_t v1 = min(v0 + kAmaxChunk / 8, n_vec);
+  uint32_t m = 0;
+#pragma unroll 4
+  for (int64_t v = v0 + threadIdx.x; v < v1; v += kAmaxThreads) {
+    const uint4 w = ptx::ld_stream_v4(x + v);
+    m = mag_max_bf16x2(mag_max_bf16x2(m, w.x), w.y);
+    m = mag_max_bf16x2(mag_max_bf16x2(m, w.z), w.w);
+  }
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  __shared__ uint32_t warp_max[kAmaxThreads / 32];
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < kAmaxThreads / 32 ? warp_max[threadIdx.x] : 0u;
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if (threadIdx.x == 0) partial[blockIdx.x] = m;
+  }
+}
+
+// One CTA: reduce the partials and write s = fp32(1/amax) * 2688.
+__global__ void __launch_bounds__(1024)
+amax_finalize_kernel(const uint32_t* __restrict__ partial, int n_partial, float* __restrict__ scale_out) {
+  uint32_t m = 0;
+  for (int i = threadIdx.x; i < n_partial; i += blockDim.x) m = max(m, partial[i]);
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  __shared__ uint32_t warp_max[32];
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < int(blockDim.x >> 5) ? warp_max[threadIdx.x] : 0u;
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    if (threadIdx.x == 0) {
+      const float amax = __uint_as_float(m << 16);
+      *scale_out = __fmul_rn(__frcp_rn(amax), 2688.0f);
+    }
+  }
+}
+
+int64_t amax_partials_needed(int64_t numel) { return (numel + kAmaxChunk - 1) / kAmaxChunk; }
+
 int launch_quantize(const void* input, const float* scale_ptr, float scale_val, int64_t numel,
                     void* output, void* output_sf, cudaStream_t stream) {
   if (numel < 0) return NVFP4_ERR_INVALID_VALUE;
@@ -163,10 +223,54 @@ int launch_dequantize(const void* input, const float* scale_ptr, float scale_val
   return status_from_cuda(cudaGetLastError());
 }
 
+int launch_quantize_auto_scale(const void* input, int64_t numel, void* output, void* output_sf,
+                               float* scale_out, uint32_t* partial, int64_t partial_capacity,
+                               cudaStream_t stream) {
+  if (numel < 0) return NVFP4_ERR_INVALID_VALUE;
+  if (numel % 16 != 0) return NVFP4_ERR_UNSUPPORTED_SHAPE;
+  if (!scale_out || !partial) return NVFP4_ERR_INVALID_VALUE;
+  const int64_t n_part = amax_partials_needed(numel);
+  if (n_part > partial_capacity) return NVFP4_ERR_TOO_LARGE;
+  if (!input || !output || !output_sf) {
+    if (numel != 0) return NVFP4_ERR_INVALID_VALUE;
+  }
+  if (numel != 0 && (!aligned_to(input, 16) || !aligned_to(output, 4))) return NVFP4_ERR_MISALIGNED;
+  if (n_part > 0) {
+    amax_partial_kernel<<<unsigned(n_part), kAmaxThreads, 0, stream>>>(
+        static_cast<const uint4*>(input), numel / 8, partial);
+  }
+  // numel == 0: amax of nothing is 0 (torch's max of an empty tensor raises; here s = inf).
+  amax_finalize_kernel<<<1, 1024, 0, stream>>>(partial, int(n_part), scale_out);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || numel == 0) return status_from_cuda(e);
+  const int64_t n_half = numel / 8;
+  const int64_t grid = (n_half + kHalfBlocksPerCta - 1) / kHalfBlocksPerCta;
+  quantize_kernel<true, true><<<unsigned(grid), kThreads, 0, stream>>>(
+      static_cast<const uint4*>(input), scale_out, 0.0f, n_half, static_cast<uint32_t*>(output),
+      static_cast<uint8_t*>(output_sf));
+  return status_from_cuda(cudaGetLastError());
+}
+
 }  // namespace
 }  // namespace nvfp4
 
 extern "C" {
+
+int64_t nvfp4_quantize_auto_scale_workspace_bytes(int64_t numel) {
+  if (numel < 0) return 0;
+  const int64_t n = nvfp4::amax_partials_needed(numel);
+  return (n > 0 ? n : 1) * int64_t(sizeof(uint32_t));
+}
+
+int nvfp4_quantize_auto_scale(const void* input, int64_t numel, void* output, void* output_sf,
+                              float* scale_out, void* workspace, int64_t workspace_bytes,
+                              cudaStream_t stream) {
+  if (!workspace || !nvfp4::aligned_to(workspace, 4)) return NVFP4_ERR_INVALID_VALUE;
+  return nvfp4::launch_quantize_auto_scale(input, numel, output, output_sf, scale_out,
+                                           static_cast<uint32_t*>(workspace),
+                                           workspace_bytes / int64_t(sizeof(uint32_t)), stream);
+}
+
 
 int nvfp4_quantize(const void* input, const float* input_scale, int64_t numel, void* output,
                    void* output_sf, cudaStream_t stream) {

@@ -71,6 +71,35 @@ std::tuple<torch::Tensor, torch::Tensor> py_quantize_nvfp4(const torch::Tensor& 
   return std::make_tuple(output, output_sf);
 }
 
+// Extension (no reference counterpart): quantize with the per-tensor scale computed on the
+// device from the input itself, s = 6*448/amax evaluated as torch evaluates the reference recipe.
+// Returns (packed, sf, s) with s a 0-dim fp32 tensor on the input's device.
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> py_quantize_nvfp4_auto_scale(
+    const torch::Tensor& input) {
+  TORCH_CHECK(input.dtype() == torch::kBFloat16 && input.is_contiguous(),
+              "input must be bf16 and contiguous");
+  TORCH_CHECK(input.device().is_cuda(), "input must be on cuda device");
+  TORCH_CHECK(input.dim() >= 1 && input.size(-1) % 16 == 0,
+              "input's last dimension must be a multiple of 16, got ", input.sizes());
+  const c10::cuda::CUDAGuard guard(input.device());
+  auto out_sizes = input.sizes().vec();
+  auto sf_sizes = input.sizes().vec();
+  out_sizes.back() /= 2;
+  sf_sizes.back() /= 16;
+  auto opts = torch::TensorOptions().device(input.device());
+  auto output = torch::empty(out_sizes, opts.dtype(torch::kUInt8));
+  auto output_sf = torch::empty(sf_sizes, opts.dtype(torch::kFloat8_e4m3fn));
+  auto scale = torch::empty({}, opts.dtype(torch::kFloat32));
+  const int64_t ws_bytes = nvfp4_quantize_auto_scale_workspace_bytes(input.numel());
+  auto ws = torch::empty({ws_bytes}, opts.dtype(torch::kUInt8));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(input.device().index());
+  check_status(nvfp4_quantize_auto_scale(input.data_ptr(), input.numel(), output.data_ptr(),
+                                         output_sf.data_ptr(), scale.data_ptr<float>(),
+                                         ws.data_ptr(), ws_bytes, stream),
+               "quantize_nvfp4_auto_scale");
+  return std::make_tuple(output, output_sf, scale);
+}
+
 torch::Tensor py_de_quantize_nvfp4(const torch::Tensor& input, const torch::Tensor& input_scale,
                                    const torch::Tensor& input_sf) {
   TORCH_CHECK(input.dtype() == torch::kUInt8 && input.is_contiguous(),
@@ -169,6 +198,9 @@ PYBIND11_MODULE(my_plugins, m) {
         py::arg("input_scale"), py::arg("input_sf"));
   m.def("gemm_nvfp4", &py_gemm_nvfp4, "gemm_nvfp4", py::arg("A"), py::arg("B"), py::arg("A_sf"),
         py::arg("B_sf"), py::arg("scale"));
+  m.def("quantize_nvfp4_auto_scale", &py_quantize_nvfp4_auto_scale,
+        "quantize with s = 6*448/amax computed on the device; returns (packed, sf, s)",
+        py::arg("input"));
   m.def("device_status", &py_device_status,
         "status word of the library's kernels on the current device (0 = OK)");
   m.def("clear_device_status", &py_clear_device_status, "reset the device status word to 0");

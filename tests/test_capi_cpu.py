@@ -53,6 +53,18 @@ def test_quantize_validation():
     assert capi.quantize_host_scale(FAKE, 1.0, 24, FAKE, FAKE) == capi.NVFP4_ERR_UNSUPPORTED_SHAPE
 
 
+def test_quantize_auto_scale_validation():
+    ws = capi.quantize_auto_scale_workspace_bytes
+    assert ws(0) == 4 and ws(16) == 4 and ws(131072) == 4 and ws(131088) == 8
+    assert ws(8192 * 8192) == 4 * 512
+    q = capi.quantize_auto_scale
+    assert q(FAKE, 24, FAKE, FAKE, FAKE, FAKE, 64) == capi.NVFP4_ERR_UNSUPPORTED_SHAPE
+    assert q(FAKE, 16, FAKE, FAKE, FAKE, None, 64) == capi.NVFP4_ERR_INVALID_VALUE
+    assert q(FAKE, 16, FAKE, FAKE, None, FAKE, 64) == capi.NVFP4_ERR_INVALID_VALUE
+    assert q(FAKE, 262144, FAKE, FAKE, FAKE, FAKE, 4) == 7  # workspace too small: TOO_LARGE
+    assert q(FAKE + 8, 16, FAKE, FAKE, FAKE, FAKE, 64) == capi.NVFP4_ERR_MISALIGNED
+
+
 def test_dequantize_validation():
     assert capi.dequantize(FAKE, FAKE, FAKE, 12, FAKE) == capi.NVFP4_ERR_UNSUPPORTED_SHAPE
     assert capi.dequantize(FAKE, FAKE, FAKE, 8, FAKE + 8) == capi.NVFP4_ERR_MISALIGNED

@@ -159,3 +159,49 @@ def test_empty_tensors(plugins):
     assert a.shape == (0, 16) and a_sf.shape == (0, 2)
     r = plugins.de_quantize_nvfp4(a, s, a_sf)
     assert r.shape == (0, 32)
+
+
+def _auto_scale_input(case):
+    g = torch.Generator(device="cuda").manual_seed(31)
+    X = torch.randn(1000, 272, device="cuda", generator=g)
+    if case == "outliers":
+        X.view(-1)[:: 197] *= 50.0
+    elif case == "zeros":
+        X.zero_()
+    elif case == "nan":
+        X[17, 5] = float("nan")
+    elif case == "inf":
+        X[999, 271] = float("-inf")
+    elif case == "tiny":
+        X *= 1e-30
+    return X.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("case", ["normal", "outliers", "zeros", "nan", "inf", "tiny"])
+def test_quantize_auto_scale_matches_torch_recipe(plugins, case):
+    """The device-computed per-tensor scale equals torch's evaluation of the reference recipe
+    (test.py:10-11) bit for bit, and the bytes equal quantize_nvfp4 with that scale."""
+    X = _auto_scale_input(case)
+    q, sf, s = plugins.quantize_nvfp4_auto_scale(X)
+    s_ref = 6 * 448 / X.abs().max().to(dtype=torch.float32)
+    assert s.shape == () and s.dtype == torch.float32 and s.device == X.device
+    if torch.isnan(s_ref):
+        assert torch.isnan(s)
+    else:
+        assert s.view(torch.int32).item() == s_ref.view(torch.int32).item(), (s.item(), s_ref.item())
+    q2, sf2 = plugins.quantize_nvfp4(X, s_ref)
+    assert torch.equal(q, q2) and torch.equal(sf.view(torch.uint8), sf2.view(torch.uint8))
+
+
+def test_quantize_auto_scale_large_activation(plugins):
+    """8192 x 8192 activation with 0.5% x50 outliers: many amax chunks, reverse traversal."""
+    g = torch.Generator(device="cuda").manual_seed(1)
+    X = torch.randn(8192, 8192, device="cuda", generator=g)
+    idx = torch.randperm(X.numel(), device="cuda", generator=g)[: int(0.005 * X.numel())]
+    X.view(-1)[idx] *= 50.0
+    X = X.to(torch.bfloat16)
+    q, sf, s = plugins.quantize_nvfp4_auto_scale(X)
+    s_ref = 6 * 448 / X.abs().max().to(dtype=torch.float32)
+    assert s.view(torch.int32).item() == s_ref.view(torch.int32).item()
+    q2, sf2 = plugins.quantize_nvfp4(X, s_ref)
+    assert torch.equal(q, q2) and torch.equal(sf.view(torch.uint8), sf2.view(torch.uint8))
