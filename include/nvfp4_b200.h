@@ -79,6 +79,21 @@ int nvfp4_quantize_auto_scale(const void* input, int64_t numel, void* output, vo
                               cudaStream_t stream);
 
 /*
+ * Allocation-free form of nvfp4_quantize_auto_scale, for callers that cannot allocate device
+ * memory (a plugin inside another runtime's enqueue where allocation is forbidden, a process
+ * whose device memory belongs to a pool it does not control, code with a fixed memory budget).
+ * No counterpart in the reference. It allocates nothing: its scratch (partial maxima) is a fixed
+ * 32 KiB device array inside this library, present on every GPU that loads it until the process
+ * exits. Inputs are limited to numel <= 2^30 elements; larger calls return NVFP4_ERR_TOO_LARGE
+ * before doing anything. The first call on a device looks up the array's device address (once
+ * per device), so make that first call outside any stream capture. All calls on a device share
+ * the array: calls that overlap on the GPU (e.g. on two streams at once) race and must be
+ * ordered by the caller. Results are identical to nvfp4_quantize_auto_scale.
+ */
+int nvfp4_quantize_auto_scale_noalloc(const void* input, int64_t numel, void* output,
+                                      void* output_sf, float* scale_out, cudaStream_t stream);
+
+/*
  * Dequantize NVFP4 -> bf16.
  * Replaces my_plugins::de_quantize_nvfp4 (csrc/quantize/quantize_nvfp4.h:7, launcher
  * csrc/quantize/quantize_nvfp4.cu:64-68). `n_bytes` is the packed byte count, as in the

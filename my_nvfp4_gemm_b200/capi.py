@@ -36,6 +36,7 @@ SIGNATURES = {
     "nvfp4_quantize_host_scale": ([_P, _F32, _I64, _P, _P, _P], _INT),
     "nvfp4_quantize_auto_scale_workspace_bytes": ([_I64], _I64),
     "nvfp4_quantize_auto_scale": ([_P, _I64, _P, _P, _P, _P, _I64, _P], _INT),
+    "nvfp4_quantize_auto_scale_noalloc": ([_P, _I64, _P, _P, _P, _P], _INT),
     "nvfp4_dequantize": ([_P, _P, _P, _I64, _P, _P], _INT),
     "nvfp4_dequantize_host_scale": ([_P, _F32, _P, _I64, _P, _P], _INT),
     "nvfp4_gemm": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P], _INT),
@@ -96,6 +97,13 @@ def quantize_auto_scale(x_ptr, numel, out_ptr, sf_ptr, scale_out_ptr, ws_ptr, ws
                         stream=0) -> int:
     return lib().nvfp4_quantize_auto_scale(x_ptr, numel, out_ptr, sf_ptr, scale_out_ptr, ws_ptr,
                                            ws_bytes, stream)
+
+
+def quantize_auto_scale_noalloc(x_ptr, numel, out_ptr, sf_ptr, scale_out_ptr, stream=0) -> int:
+    """Same result as quantize_auto_scale, with the library's own fixed device scratch instead
+    of a caller workspace (inputs up to 2^30 elements; see include/nvfp4_b200.h)."""
+    return lib().nvfp4_quantize_auto_scale_noalloc(x_ptr, numel, out_ptr, sf_ptr, scale_out_ptr,
+                                                   stream)
 
 
 def dequantize(q_ptr, scale_ptr, sf_ptr, n_bytes, out_ptr, stream=0) -> int:

@@ -13,6 +13,7 @@
 // stores), four independent half-blocks per thread keep loads in flight, and the scale is read
 // from device memory so no host synchronisation is needed.
 #include <cstdint>
+#include <mutex>
 
 #include "capi_util.h"
 #include "ptx.cuh"
@@ -251,10 +252,53 @@ int launch_quantize_auto_scale(const void* input, int64_t numel, void* output, v
   return status_from_cuda(cudaGetLastError());
 }
 
+// ---- allocation-free form of the per-tensor-scale quantize -------------------------------
+// Some callers cannot allocate device memory at all: a plugin running inside another runtime's
+// enqueue call where allocation is forbidden, a process whose device memory is owned entirely
+// by a pool it does not control, or code with a fixed memory budget fixed before it runs. For
+// them the partial maxima live in a file-scope device array instead of a caller workspace.
+// It is a fixed 32 KiB on every GPU that loads this library, until the process exits.
+constexpr int64_t kNoAllocMaxPartials = 8192;  // one per 128 Ki elements: inputs up to 2^30
+static __device__ __align__(256) uint32_t g_noalloc_amax_partials[kNoAllocMaxPartials];
+constexpr int kNoAllocMaxDevices = 64;
+
+// The array's name is only a stand-in in host code; its device address must be looked up with
+// the device current. Done once per device, on the first call there (which therefore should not
+// be inside a stream capture).
+int noalloc_partials(uint32_t** out) {
+  static std::once_flag flags[kNoAllocMaxDevices];
+  static uint32_t* addr[kNoAllocMaxDevices];
+  static cudaError_t errs[kNoAllocMaxDevices];
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
+    return NVFP4_ERR_NO_DEVICE;
+  std::call_once(flags[dev], [&] {
+    void* ptr = nullptr;
+    errs[dev] = cudaGetSymbolAddress(&ptr, g_noalloc_amax_partials);
+    addr[dev] = static_cast<uint32_t*>(ptr);
+  });
+  if (errs[dev] != cudaSuccess || addr[dev] == nullptr) return NVFP4_ERR_CUDA;
+  *out = addr[dev];
+  return NVFP4_OK;
+}
+
 }  // namespace
 }  // namespace nvfp4
 
 extern "C" {
+
+int nvfp4_quantize_auto_scale_noalloc(const void* input, int64_t numel, void* output,
+                                      void* output_sf, float* scale_out, cudaStream_t stream) {
+  if (numel > nvfp4::kNoAllocMaxPartials * nvfp4::kAmaxChunk) return NVFP4_ERR_TOO_LARGE;
+  uint32_t* partials = nullptr;
+  const int st = nvfp4::noalloc_partials(&partials);
+  if (st != NVFP4_OK) return st;
+  // Every partial the finalize pass reads is written by this call's amax pass first, so nothing
+  // in the array has to start at zero or be cleared between calls.
+  return nvfp4::launch_quantize_auto_scale(input, numel, output, output_sf, scale_out, partials,
+                                           nvfp4::kNoAllocMaxPartials, stream);
+}
+
 
 int64_t nvfp4_quantize_auto_scale_workspace_bytes(int64_t numel) {
   if (numel < 0) return 0;
