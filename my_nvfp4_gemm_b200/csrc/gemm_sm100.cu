@@ -13,9 +13,11 @@
 //               rows of A and its own 128-row half of B, the leader issues M=256 MMAs that read
 //               both CTAs' shared memory and accumulate into both CTAs' tensor memory; per-SM
 //               operand traffic per FLOP drops by a third and the ring is one stage deeper;
-//   * warp-specialised (320 threads per CTA):
-//       warp 8  TMA producer: A/B tiles (128B-swizzled) and scale-factor tiles into a
-//               STAGES-deep shared-memory ring, guarded by full and empty mbarriers;
+//   * warp-specialised (352 threads per CTA):
+//       warp 8  TMA producer of the A/B tiles (128B-swizzled) into a STAGES-deep shared-memory
+//               ring, guarded by full and empty mbarriers;
+//       warp 10 TMA producer of the scale-factor tiles into their own ring (up to 64 bytes of
+//               every row per load, so whole sectors are fetched);
 //       warps 0-3 scale-factor writers: read the API's row-major UE4M3 factors from shared
 //               memory and write them with tcgen05.st into the stage's tensor-memory slot, in
 //               the lane/column layout the block-scaled MMA reads (one warp per lane quarter);
@@ -50,18 +52,29 @@ constexpr int kSfBytesPerRow = kBK / 16;  // 16 scale bytes per row per stage
 constexpr int kNumSfWarps = 4;            // warps 0-3: scale-factor writers (TMEM quarters 0-3)
 constexpr int kFirstEpiWarp = 4;          // warps 4-7: epilogue (TMEM quarters 0-3)
 constexpr int kNumEpiWarps = 4;
-constexpr int kProducerWarp = 8;          // TMA producer
+constexpr int kProducerWarp = 8;          // TMA producer of the A/B tiles
 constexpr int kMmaWarp = 9;               // MMA issuer, owns the TMEM allocation
-constexpr int kThreads = 32 * 10;
+constexpr int kSfProducerWarp = 10;       // TMA producer of the scale-factor tiles
+constexpr int kThreads = 32 * 11;
 constexpr int kEpiCols = 32;              // accumulator columns per epilogue store
 constexpr int kEpiBufBytes = 32 * kEpiCols * 2;  // 32 rows x 32 bf16 per epilogue warp
 
-template <int BN_, int STAGES_, int ACC_STAGES_, bool PAIR_>
+// Scale factors have their own shared-memory ring of SF_SLOTS slots, filled by their own
+// producer warp. One slot holds SF_KB consecutive k-blocks (16 * SF_KB bytes of every row): the
+// API's row-major factors are 16 bytes per row per k-block with rows K/16 bytes apart, so a
+// 16-byte box row would fetch half of a 32-byte sector per request; 64-byte rows (SF_KB = 4)
+// use whole sectors and a quarter of the requests. Rows of 32 or 64 bytes are swizzled by the
+// TMA unit so that the writers' 16-byte reads stay free of bank conflicts.
+template <int BN_, int STAGES_, int ACC_STAGES_, bool PAIR_, int SF_KB_, int SF_SLOTS_>
 struct Cfg {
   static constexpr int BN = BN_;
   static constexpr int STAGES = STAGES_;
   static constexpr int ACC_STAGES = ACC_STAGES_;
   static constexpr bool PAIR = PAIR_;
+  static constexpr int SF_KB = SF_KB_;                     // k-blocks per scale-factor slot
+  static constexpr int SF_SLOTS = SF_SLOTS_;
+  static constexpr int SF_ROW_BYTES = kSfBytesPerRow * SF_KB;
+  static_assert(SF_KB == 1 || SF_KB == 2 || SF_KB == 4, "SF_KB must be 1, 2 or 4");
   static constexpr int CTAS = PAIR ? 2 : 1;
   static constexpr int TILE_M = kRowsPerCta * CTAS;        // output rows per tile
   static constexpr int B_ROWS = BN / CTAS;                 // B rows each CTA loads
@@ -69,26 +82,26 @@ struct Cfg {
 
   static constexpr int A_STAGE = kRowsPerCta * kBKBytes;   // 16 KiB
   static constexpr int B_STAGE = B_ROWS * kBKBytes;
-  static constexpr int SFA_STAGE = kRowsPerCta * kSfBytesPerRow;   // 2 KiB
-  static constexpr int SFB_STAGE = BN * kSfBytesPerRow;    // every CTA holds all BN rows
+  static constexpr int SFA_SLOT = kRowsPerCta * SF_ROW_BYTES;
+  static constexpr int SFB_SLOT = BN * SF_ROW_BYTES;       // every CTA holds all BN rows
   static constexpr uint32_t AB_TX = uint32_t(CTAS) * (A_STAGE + B_STAGE);  // pair total
-  static constexpr uint32_t SF_TX = SFA_STAGE + SFB_STAGE;                 // per CTA
+  static constexpr uint32_t SF_TX = SFA_SLOT + SFB_SLOT;                   // per CTA
 
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
   static constexpr int OFF_SFA = OFF_B + STAGES * B_STAGE;
-  static constexpr int OFF_SFB = OFF_SFA + STAGES * SFA_STAGE;
-  static constexpr int OFF_EPI = OFF_SFB + STAGES * SFB_STAGE;
+  static constexpr int OFF_SFB = OFF_SFA + SF_SLOTS * SFA_SLOT;
+  static constexpr int OFF_EPI = OFF_SFB + SF_SLOTS * SFB_SLOT;
   static constexpr int OFF_BAR = OFF_EPI + kNumEpiWarps * kEpiBufBytes;
-  static constexpr int NUM_BARS = 4 * STAGES + 2 * ACC_STAGES + 1;
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * SF_SLOTS + 2 * ACC_STAGES + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;     // slack to align the base to 1 KiB
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget exceeded");
 
   // Tensor memory columns: accumulators, then one scale-factor slot per pipeline stage, so the
-  // factors of stage s+1 are written while the MMAs of stage s still read theirs. Within a slot:
-  // B's factors for K-steps 0..3 (BN/32 columns each), then A's (4 columns each).
+  // factors of later fills are written while the MMAs of earlier ones still read theirs. Within
+  // a slot: B's factors for K-steps 0..3 (BN/32 columns each), then A's (4 columns each).
   static constexpr uint32_t SFB_COLS_PER_STEP = BN / 32;
   static constexpr uint32_t SF_SLOT_COLS = kKSteps * (4 + SFB_COLS_PER_STEP);
   static constexpr uint32_t COL_SF = BN * ACC_STAGES;
@@ -109,27 +122,51 @@ struct Params {
   uint64_t timeout_ns;
 };
 
+// Tile order: the M x N tile grid is walked in bands of kGroupM tile rows, column by column
+// within a band, so the tiles the persistent CTAs work on at any moment share a narrow band of
+// A rows and a few B column blocks in L2.
+constexpr int kGroupM = 16;
+
+__device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, int& nb) {
+  const int per_band = kGroupM * p.n_blocks;
+  const int band = tile / per_band;
+  const int first = band * kGroupM;
+  const int rows = min(p.m_blocks - first, kGroupM);
+  const int r = tile - band * per_band;
+  mb = first + r % rows;
+  nb = r / rows;
+}
+
 // Scale-factor writer (one warp per TMEM lane quarter q). The block-scaled MMA of sub-partition
 // q reads the scale factors of A row 32q+r from TMEM lane 32q+r, column sfa+q, and those of B
 // row n from lane 32q+(n%32), column sfb+n/32 (B's factors are needed by every quarter). The
-// warp reads its rows' row-major factors from the stage's shared-memory tile (16 bytes per row
-// = K-steps 0..3) and writes its quarter of the stage's TMEM slot with tcgen05.st:
+// warp reads its rows' factors for k-block c of the shared-memory slot (16 bytes per row =
+// K-steps 0..3) and writes its quarter of the stage's TMEM slot with tcgen05.st:
 //   slot + j*(BN/32) + i   <- step-j word of B row 32i + lane     (BN/8 columns)
 //   slot + BN/8 + 4j + k   <- step-j word of A row 32q + lane     (16 columns, k = 0..3)
+//
+// Shared-memory address of k-block c's 16 bytes of row `row` in a scale-factor slot. The TMA
+// unit's 32B/64B swizzle XORs the 16-byte chunk index with address bits 7 and up of the row.
 template <class C>
-__device__ __forceinline__ void write_sf_slot(uint32_t slot, uint32_t sfa_s, uint32_t sfb_s, int q,
-                                              int lane) {
+__device__ __forceinline__ uint32_t sf_chunk_addr(uint32_t base, int row, int c) {
+  const int sw = (row * C::SF_KB / 8) % C::SF_KB;
+  return base + uint32_t(row * C::SF_ROW_BYTES + ((c ^ sw) << 4));
+}
+
+template <class C>
+__device__ __forceinline__ void write_sf_slot(uint32_t slot, uint32_t sfa_s, uint32_t sfb_s, int c,
+                                              int q, int lane) {
   constexpr int kChunksB = C::BN / 32;
   uint32_t vb[C::BN / 8];
 #pragma unroll
   for (int i = 0; i < kChunksB; ++i) {
-    const uint4 w = ptx::ld_shared_v4(sfb_s + uint32_t(32 * i + lane) * 16);
+    const uint4 w = ptx::ld_shared_v4(sf_chunk_addr<C>(sfb_s, 32 * i + lane, c));
     vb[0 * kChunksB + i] = w.x;
     vb[1 * kChunksB + i] = w.y;
     vb[2 * kChunksB + i] = w.z;
     vb[3 * kChunksB + i] = w.w;
   }
-  const uint4 a = ptx::ld_shared_v4(sfa_s + uint32_t(32 * q + lane) * 16);
+  const uint4 a = ptx::ld_shared_v4(sf_chunk_addr<C>(sfa_s, 32 * q + lane, c));
   uint32_t va[16];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
@@ -162,11 +199,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   uint8_t* sSFB = smem + C::OFF_SFB;
   uint8_t* sEPI = smem + C::OFF_EPI;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* full_bar = bars;                        // A/B landed (leader's counts the pair)
-  uint64_t* sfload_bar = bars + C::STAGES;          // this CTA's scale-factor tiles landed
-  uint64_t* sf_bar = bars + 2 * C::STAGES;          // scale factors in TMEM (leader's, all CTAs)
-  uint64_t* empty_bar = bars + 3 * C::STAGES;       // MMA done with the stage -> producer
-  uint64_t* tfull_bar = bars + 4 * C::STAGES;       // accumulator ready -> epilogue
+  // full[s] (the leader's) completes when the stage's A/B tiles of both CTAs have landed (the
+  // producer's expect-tx arrival plus the bytes) and every writer warp of both CTAs has put
+  // the stage's scale factors into tensor memory: one barrier for the MMA warp to poll.
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + C::STAGES;           // MMAs done with the stage -> producers
+  uint64_t* sfull_bar = bars + 2 * C::STAGES;       // this CTA's scale-factor slot landed
+  uint64_t* sempty_bar = sfull_bar + C::SF_SLOTS;   // writers done reading the slot
+  uint64_t* tfull_bar = sempty_bar + C::SF_SLOTS;   // accumulator ready -> epilogue
   uint64_t* tempty_bar = tfull_bar + C::ACC_STAGES; // accumulator drained -> MMA (leader's)
   uint64_t* drain_bar = tempty_bar + C::ACC_STAGES; // MMA drain before TMEM free
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
@@ -181,10 +221,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
-      ptx::mbar_init(&full_bar[i], 1);
-      ptx::mbar_init(&sfload_bar[i], 1);
-      ptx::mbar_init(&sf_bar[i], kNumSfWarps * C::CTAS);
+      ptx::mbar_init(&full_bar[i], 1 + kNumSfWarps * C::CTAS);
       ptx::mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < C::SF_SLOTS; ++i) {
+      ptx::mbar_init(&sfull_bar[i], 1);
+      ptx::mbar_init(&sempty_bar[i], kNumSfWarps);
     }
     for (int i = 0; i < C::ACC_STAGES; ++i) {
       ptx::mbar_init(&tfull_bar[i], 1);
@@ -215,11 +257,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int64_t fills = 0;
       for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
-        const int m_cta = (tile % p.m_blocks) * C::TILE_M + int(rank) * kRowsPerCta;
-        const int n0 = (tile / p.m_blocks) * C::BN;
-        const int n_cta = n0 + int(rank) * C::B_ROWS;
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        const int m_cta = mb * C::TILE_M + int(rank) * kRowsPerCta;
+        const int n_cta = nb * C::BN + int(rank) * C::B_ROWS;
         for (int kb = 0; kb < p.k_stages; ++kb) {
           if (!ptx::mbar_wait<kPair>(&empty_bar[stage], phase ^ 1, abort_flag, p.timeout_ns))
             goto producer_done;
@@ -231,39 +273,68 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
             ptx::tma_load_2d(sA + stage * C::A_STAGE, &tm_a, &full_bar[stage], kb * kBKBytes, m_cta);
             ptx::tma_load_2d(sB + stage * C::B_STAGE, &tm_b, &full_bar[stage], kb * kBKBytes, n_cta);
           }
-          ptx::mbar_arrive_expect_tx(&sfload_bar[stage], C::SF_TX);
-          ptx::tma_load_2d(sSFA + stage * C::SFA_STAGE, &tm_sfa, &sfload_bar[stage], kb * kSfBytesPerRow, m_cta);
-          ptx::tma_load_2d(sSFB + stage * C::SFB_STAGE, &tm_sfb, &sfload_bar[stage], kb * kSfBytesPerRow, n0);
-          ++fills;
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
         }
       }
     producer_done:
-      // Never leave a TMA write in flight into shared memory of an exiting CTA: wait (bounded,
-      // ignoring the abort flag) until the most recent fill of every slot has landed. In a pair
-      // the A/B bytes of both CTAs are counted on the leader's barriers; the follower waits a
-      // fixed bounded time after an abort instead.
+      // Never leave a TMA write in flight into shared memory of an exiting CTA. Without an
+      // abort, the MMA warp has consumed every fill, so every copy has landed. After an abort
+      // the full barriers may never complete (they also count the writer warps, which stop), so
+      // wait a fixed bounded time, far above a copy's latency, instead.
+      if (*abort_flag) {
+        const uint64_t t0 = ptx::globaltimer_ns();
+        while (ptx::globaltimer_ns() - t0 < 1000000ull) {
+        }
+      }
+    }
+  } else if (warp == kSfProducerWarp) {
+    // ------------------------------------------------------------------ scale-factor producer
+    // Slot loads of SF_KB k-blocks of this CTA's A rows and all BN B rows, as far ahead of the
+    // writers as the SF_SLOTS-deep ring allows (each CTA of a pair loads its own).
+    if (lane == 0) {
+      int slot = 0;
+      uint32_t phase = 0;
+      int64_t loads = 0;
+      for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        const int row_a = mb * C::TILE_M + int(rank) * kRowsPerCta;
+        const int row_b = nb * C::BN;
+        for (int kb = 0; kb < p.k_stages; kb += C::SF_KB) {
+          if (!ptx::mbar_wait<kPair>(&sempty_bar[slot], phase ^ 1, abort_flag, p.timeout_ns))
+            goto sf_producer_done;
+          ptx::mbar_arrive_expect_tx(&sfull_bar[slot], C::SF_TX);
+          ptx::tma_load_2d(sSFA + slot * C::SFA_SLOT, &tm_sfa, &sfull_bar[slot],
+                           kb * kSfBytesPerRow, row_a);
+          ptx::tma_load_2d(sSFB + slot * C::SFB_SLOT, &tm_sfb, &sfull_bar[slot],
+                           kb * kSfBytesPerRow, row_b);
+          ++loads;
+          if (++slot == C::SF_SLOTS) { slot = 0; phase ^= 1; }
+        }
+      }
+    sf_producer_done:
       {
         int no_abort = 0;
-        const int64_t last = fills < C::STAGES ? fills : C::STAGES;
+        const int64_t last = loads < C::SF_SLOTS ? loads : C::SF_SLOTS;
         for (int64_t i = 0; i < last; ++i) {
-          const int64_t f = fills - 1 - i;
-          const uint32_t par = uint32_t((f / C::STAGES) & 1);
-          ptx::mbar_wait<kPair>(&sfload_bar[f % C::STAGES], par, &no_abort, p.timeout_ns);
-          if (rank == 0)
-            ptx::mbar_wait<kPair>(&full_bar[f % C::STAGES], par, &no_abort, p.timeout_ns);
-        }
-        if (kPair && rank != 0 && *abort_flag) {
-          const uint64_t t0 = ptx::globaltimer_ns();
-          while (ptx::globaltimer_ns() - t0 < 1000000ull) {
-          }
+          const int64_t g = loads - 1 - i;
+          ptx::mbar_wait<kPair>(&sfull_bar[g % C::SF_SLOTS], uint32_t((g / C::SF_SLOTS) & 1),
+                                &no_abort, p.timeout_ns);
         }
       }
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0 && rank == 0) {
+      // The tensor pipe does not let this thread run ahead of it: every instruction between two
+      // MMAs delays the next one. So the loop polls one barrier per k-block and advances
+      // precomputed descriptors and TMEM addresses by constants.
       constexpr uint32_t idesc = ptx::make_idesc_mxf4nvf4(C::TILE_M, C::BN);
+      constexpr uint32_t kADescStep = C::A_STAGE >> 4;   // descriptor start-address units
+      constexpr uint32_t kBDescStep = C::B_STAGE >> 4;
+      const uint64_t a_desc0 = ptx::make_smem_desc(ptx::smem_u32(sA), 0, 1024, ptx::kLayoutSW128);
+      const uint64_t b_desc0 = ptx::make_smem_desc(ptx::smem_u32(sB), 0, 1024, ptx::kLayoutSW128);
+      const uint32_t t_sf0 = tmem_base + C::COL_SF;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -274,28 +345,28 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         ptx::tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * C::BN);
         for (int kb = 0; kb < p.k_stages; ++kb) {
-          if (!ptx::mbar_wait<kPair>(&sf_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
           if (!ptx::mbar_wait<kPair>(&full_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
           ptx::tc_fence_after_sync();
-          const uint32_t t_sfb = tmem_base + C::COL_SF + uint32_t(stage) * C::SF_SLOT_COLS;
+          const uint64_t a_desc = a_desc0 + uint32_t(stage) * kADescStep;
+          const uint64_t b_desc = b_desc0 + uint32_t(stage) * kBDescStep;
+          const uint32_t t_sfb = t_sf0 + uint32_t(stage) * C::SF_SLOT_COLS;
           const uint32_t t_sfa = t_sfb + C::BN / 8;
-          const uint32_t a_s = ptx::smem_u32(sA + stage * C::A_STAGE);
-          const uint32_t b_s = ptx::smem_u32(sB + stage * C::B_STAGE);
+          // K-step j starts 32 bytes (2 descriptor units) further along the swizzled rows.
+          if constexpr (kPair) {
+            ptx::tc_mma_mxf4nvf4_pair(d_tmem, a_desc, b_desc, idesc, t_sfa, t_sfb, kb != 0 ? 1u : 0u);
 #pragma unroll
-          for (int j = 0; j < kKSteps; ++j) {
-            // K-step j starts 32 bytes further along the 128-byte swizzled rows.
-            const uint64_t a_desc = ptx::make_smem_desc(a_s + j * 32, 0, 1024, ptx::kLayoutSW128);
-            const uint64_t b_desc = ptx::make_smem_desc(b_s + j * 32, 0, 1024, ptx::kLayoutSW128);
-            if constexpr (kPair)
-              ptx::tc_mma_mxf4nvf4_pair(d_tmem, a_desc, b_desc, idesc, t_sfa + 4 * j,
-                                        t_sfb + j * (C::BN / 32), (kb | j) != 0 ? 1u : 0u);
-            else
-              ptx::tc_mma_mxf4nvf4(d_tmem, a_desc, b_desc, idesc, t_sfa + 4 * j,
-                                   t_sfb + j * (C::BN / 32), (kb | j) != 0 ? 1u : 0u);
+            for (int j = 1; j < kKSteps; ++j)
+              ptx::tc_mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * j, b_desc + 2 * j, idesc, t_sfa + 4 * j,
+                                        t_sfb + j * (C::BN / 32), 1u);
+            ptx::tc_commit_pair(&empty_bar[stage], 0x3);  // stage free in both CTAs
+          } else {
+            ptx::tc_mma_mxf4nvf4(d_tmem, a_desc, b_desc, idesc, t_sfa, t_sfb, kb != 0 ? 1u : 0u);
+#pragma unroll
+            for (int j = 1; j < kKSteps; ++j)
+              ptx::tc_mma_mxf4nvf4(d_tmem, a_desc + 2 * j, b_desc + 2 * j, idesc, t_sfa + 4 * j,
+                                   t_sfb + j * (C::BN / 32), 1u);
+            ptx::tc_commit(&empty_bar[stage]);
           }
-          // frees the stage's smem and TMEM scale slot (in both CTAs of a pair)
-          if constexpr (kPair) ptx::tc_commit_pair(&empty_bar[stage], 0x3);
-          else ptx::tc_commit(&empty_bar[stage]);
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
         }
         if constexpr (kPair) ptx::tc_commit_pair(&tfull_bar[acc], 0x3);
@@ -313,25 +384,39 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     }
   } else if (warp < kNumSfWarps) {
     // ------------------------------------------------------------------ scale-factor writers
-    // Stage s's TMEM slot is rewritten only after sfload[s] of its next fill, which the
-    // producer issues after empty[s]: the MMAs that read the slot's previous contents are done.
+    // Fill f = (tile, kb) uses k-block c = kb % SF_KB of the current scale-factor slot. Its
+    // factors go to the TMEM slot of stage f % STAGES once (1) the shared-memory slot has landed
+    // (waited for at its first k-block) and (2) the MMAs of fill f - STAGES, which read the TMEM
+    // slot's previous contents, are done (the empty phase the A/B producer also waits for).
+    // After the slot's last k-block of the tile, the slot goes back to the scale-factor
+    // producer.
     const int q = warp;
     const uint32_t lane_base = uint32_t(q * 32) << 16;
     int stage = 0;
     uint32_t phase = 0;
+    int slot = 0;
+    uint32_t slot_phase = 0;
     for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
       for (int kb = 0; kb < p.k_stages; ++kb) {
-        const bool ok = ptx::mbar_wait<kPair>(&sfload_bar[stage], phase, abort_flag, p.timeout_ns);
+        const int c = kb % C::SF_KB;
+        bool ok = true;
+        if (c == 0) ok = ptx::mbar_wait<kPair>(&sfull_bar[slot], slot_phase, abort_flag, p.timeout_ns);
+        if (ok) ok = ptx::mbar_wait<kPair>(&empty_bar[stage], phase ^ 1, abort_flag, p.timeout_ns);
         if (!__all_sync(0xFFFFFFFFu, ok)) goto sf_done;
+        ptx::tc_fence_after_sync();
         write_sf_slot<C>(tmem_base + lane_base + C::COL_SF + uint32_t(stage) * C::SF_SLOT_COLS,
-                         ptx::smem_u32(sSFA + stage * C::SFA_STAGE),
-                         ptx::smem_u32(sSFB + stage * C::SFB_STAGE), q, lane);
+                         ptx::smem_u32(sSFA + slot * C::SFA_SLOT),
+                         ptx::smem_u32(sSFB + slot * C::SFB_SLOT), c, q, lane);
         ptx::tmem_wait_st();
         ptx::tc_fence_before_sync();
         __syncwarp();
         if (lane == 0) {
-          if constexpr (kPair) ptx::mbar_arrive_cta(&sf_bar[stage], 0);
-          else ptx::mbar_arrive(&sf_bar[stage]);
+          if constexpr (kPair) ptx::mbar_arrive_cta(&full_bar[stage], 0);
+          else ptx::mbar_arrive(&full_bar[stage]);
+        }
+        if (c == C::SF_KB - 1 || kb == p.k_stages - 1) {
+          if (lane == 0) ptx::mbar_arrive(&sempty_bar[slot]);
+          if (++slot == C::SF_SLOTS) { slot = 0; slot_phase ^= 1; }
         }
         if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
       }
@@ -348,8 +433,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
-      const int m_cta = (tile % p.m_blocks) * C::TILE_M + int(rank) * kRowsPerCta;
-      const int n0 = (tile / p.m_blocks) * C::BN;
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      const int m_cta = mb * C::TILE_M + int(rank) * kRowsPerCta;
+      const int n0 = nb * C::BN;
       const bool ok = ptx::mbar_wait<kPair>(&tfull_bar[acc], acc_phase, abort_flag, p.timeout_ns);
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
       ptx::tc_fence_after_sync();
@@ -512,8 +599,12 @@ int resident_units(int dev) {
   return units[dev];
 }
 
-using CfgSingle = Cfg<256, 4, 1, false>;  // 128 x 256 tiles, one CTA, 4-stage ring
-using CfgPair = Cfg<256, 5, 1, true>;     // 256 x 256 tiles, CTA pair, 5-stage ring per CTA
+// 128 x 256 tiles, one CTA: 4-stage A/B ring, scale factors one k-block per shared-memory slot
+// (4 slots).
+using CfgSingle = Cfg<256, 4, 1, false, 1, 4>;
+// 256 x 256 tiles, CTA pair: 5-stage A/B ring per CTA (160 KiB), scale factors four k-blocks
+// per shared-memory slot (64-byte rows, 2 slots); tensor memory 256 + 5 x 48 columns.
+using CfgPair = Cfg<256, 5, 1, true, 4, 2>;
 
 template <class C>
 int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
@@ -526,14 +617,18 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
 
   CUtensorMap tm_a, tm_b, tm_sfa, tm_sfb, tm_d;
   const uint64_t kb = uint64_t(K) / 2, ks = uint64_t(K) / 16;
+  // Scale-factor rows of 16/32/64 bytes per slot; the wider ones swizzled (see sf_chunk_addr).
+  const CUtensorMapSwizzle sf_swizzle = C::SF_ROW_BYTES == 64   ? CU_TENSOR_MAP_SWIZZLE_64B
+                                        : C::SF_ROW_BYTES == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                                : CU_TENSOR_MAP_SWIZZLE_NONE;
   bool ok = make_map_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, kb, M, kb, kBKBytes, kRowsPerCta,
                         CU_TENSOR_MAP_SWIZZLE_128B) &&
             make_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, B, kb, N, kb, kBKBytes, C::B_ROWS,
                         CU_TENSOR_MAP_SWIZZLE_128B) &&
-            make_map_2d(&tm_sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, A_sf, ks, M, ks, kSfBytesPerRow,
-                        kRowsPerCta, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-            make_map_2d(&tm_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, B_sf, ks, N, ks, kSfBytesPerRow,
-                        C::BN, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+            make_map_2d(&tm_sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, A_sf, ks, M, ks, C::SF_ROW_BYTES,
+                        kRowsPerCta, sf_swizzle) &&
+            make_map_2d(&tm_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, B_sf, ks, N, ks, C::SF_ROW_BYTES,
+                        C::BN, sf_swizzle) &&
             make_map_2d(&tm_d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, D, N, M, uint64_t(N) * 2,
                         kEpiCols, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (!ok) return encode_fn() ? NVFP4_ERR_INVALID_VALUE : NVFP4_ERR_NO_DEVICE;
@@ -548,6 +643,7 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
   p.k_stages = int(K / kBK);
   p.timeout_ns = 2000000000ull;  // 2 s per wait: far above any legitimate stall
   const int64_t tiles = int64_t(p.m_blocks) * p.n_blocks;
+  if (tiles > 0x7FFFFFFF / 2) return NVFP4_ERR_TOO_LARGE;
   const int grid_units = int(tiles < units ? tiles : units);
   if constexpr (C::PAIR) {
     cudaLaunchConfig_t cfg = {};
