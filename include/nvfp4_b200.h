@@ -131,6 +131,25 @@ int nvfp4_gemm_host_scale(const void* A, const void* B, const void* A_sf, const 
                           cudaStream_t stream);
 
 /*
+ * Scale factors in the 128x4 blocked layout that library block-scaled GEMMs consume (cuBLASLt's
+ * block-scaling-factor layout; torch._scaled_mm with float4_e2m1fn_x2 operands). No reference
+ * counterpart: the reference's factors only feed its own kernel. Row-major sf[rows][cols]
+ * (cols = K/16 UE4M3 bytes per row, as every entry point above produces) <-> blocked: rows
+ * padded to a multiple of 128 and cols to a multiple of 4 with zero bytes, cut into 128x4
+ * blocks stored row-block-major; inside a block, row 32*i + j and column c sit at byte
+ * 16*j + 4*i + c.
+ *   nvfp4_blocked_scale_bytes: size of the blocked buffer (-1 for negative sizes)
+ *   nvfp4_scale_to_blocked   : sf (any alignment) -> blocked (16-byte aligned, full size)
+ *   nvfp4_scale_from_blocked : blocked (16-byte aligned) -> sf; padding is dropped
+ * Sizes beyond 4,194,240 columns return NVFP4_ERR_TOO_LARGE.
+ */
+int64_t nvfp4_blocked_scale_bytes(int64_t rows, int64_t cols);
+int nvfp4_scale_to_blocked(const void* sf, int64_t rows, int64_t cols, void* blocked,
+                           cudaStream_t stream);
+int nvfp4_scale_from_blocked(const void* blocked, int64_t rows, int64_t cols, void* sf,
+                             cudaStream_t stream);
+
+/*
  * Device-side status word, shared by all kernels of this library on the current device.
  * Kernels that wait on barriers give up after a bounded time, record
  * NVFP4_ERR_DEVICE_TIMEOUT here and return instead of hanging. Reading synchronises `stream`.

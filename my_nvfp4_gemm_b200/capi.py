@@ -41,6 +41,9 @@ SIGNATURES = {
     "nvfp4_dequantize_host_scale": ([_P, _F32, _P, _I64, _P, _P], _INT),
     "nvfp4_gemm": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P], _INT),
     "nvfp4_gemm_host_scale": ([_P, _P, _P, _P, _F32, _P, _I64, _I64, _I64, _P], _INT),
+    "nvfp4_blocked_scale_bytes": ([_I64, _I64], _I64),
+    "nvfp4_scale_to_blocked": ([_P, _I64, _I64, _P, _P], _INT),
+    "nvfp4_scale_from_blocked": ([_P, _I64, _I64, _P, _P], _INT),
     "nvfp4_device_status": ([ctypes.POINTER(_INT), _P], _INT),
     "nvfp4_clear_device_status": ([_P], _INT),
     "nvfp4_selftest_wait_timeout": ([_U64, _P], _INT),
@@ -120,6 +123,18 @@ def gemm(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, d_ptr, m, n, k, stream=0) ->
 
 def gemm_host_scale(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale, d_ptr, m, n, k, stream=0) -> int:
     return lib().nvfp4_gemm_host_scale(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale, d_ptr, m, n, k, stream)
+
+
+def blocked_scale_bytes(rows, cols) -> int:
+    return lib().nvfp4_blocked_scale_bytes(rows, cols)
+
+
+def scale_to_blocked(sf_ptr, rows, cols, blocked_ptr, stream=0) -> int:
+    return lib().nvfp4_scale_to_blocked(sf_ptr, rows, cols, blocked_ptr, stream)
+
+
+def scale_from_blocked(blocked_ptr, rows, cols, sf_ptr, stream=0) -> int:
+    return lib().nvfp4_scale_from_blocked(blocked_ptr, rows, cols, sf_ptr, stream)
 
 
 def device_status(stream=0) -> int:

@@ -183,6 +183,45 @@ int64_t py_device_status() {
   return v;
 }
 
+// Extension (no reference counterpart): scale factors in the 128x4 blocked layout that library
+// block-scaled GEMMs consume. `sf` [..., cols] (float8_e4m3fn or uint8, contiguous, CUDA); all
+// leading dimensions are rows. Returns a 1-D float8_e4m3fn tensor of
+// round_up(rows, 128) * round_up(cols, 4) bytes.
+torch::Tensor py_swizzle_scale_factors(const torch::Tensor& sf) {
+  TORCH_CHECK((sf.dtype() == torch::kFloat8_e4m3fn || sf.dtype() == torch::kUInt8) &&
+                  sf.is_contiguous(),
+              "sf must be float8_e4m3fn (or uint8) and contiguous");
+  TORCH_CHECK(sf.device().is_cuda(), "sf must be on cuda device");
+  TORCH_CHECK(sf.dim() >= 1, "sf must have at least one dimension");
+  const c10::cuda::CUDAGuard guard(sf.device());
+  const int64_t cols = sf.size(-1);
+  const int64_t rows = cols == 0 ? 0 : sf.numel() / cols;
+  const int64_t bytes = nvfp4_blocked_scale_bytes(rows, cols);
+  auto out = torch::empty({bytes}, torch::dtype(torch::kFloat8_e4m3fn).device(sf.device()));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(sf.device().index());
+  check_status(nvfp4_scale_to_blocked(sf.data_ptr(), rows, cols, out.data_ptr(), stream),
+               "swizzle_scale_factors");
+  return out;
+}
+
+// Inverse of swizzle_scale_factors: blocked (1-D, CUDA) -> float8_e4m3fn [rows, cols].
+torch::Tensor py_unswizzle_scale_factors(const torch::Tensor& blocked, int64_t rows, int64_t cols) {
+  TORCH_CHECK((blocked.dtype() == torch::kFloat8_e4m3fn || blocked.dtype() == torch::kUInt8) &&
+                  blocked.is_contiguous(),
+              "blocked must be float8_e4m3fn (or uint8) and contiguous");
+  TORCH_CHECK(blocked.device().is_cuda(), "blocked must be on cuda device");
+  TORCH_CHECK(rows >= 0 && cols >= 0, "rows and cols must be non-negative");
+  TORCH_CHECK(blocked.numel() == nvfp4_blocked_scale_bytes(rows, cols),
+              "blocked holds ", blocked.numel(), " bytes, expected ",
+              nvfp4_blocked_scale_bytes(rows, cols), " for ", rows, " x ", cols);
+  const c10::cuda::CUDAGuard guard(blocked.device());
+  auto out = torch::empty({rows, cols}, torch::dtype(torch::kFloat8_e4m3fn).device(blocked.device()));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(blocked.device().index());
+  check_status(nvfp4_scale_from_blocked(blocked.data_ptr(), rows, cols, out.data_ptr(), stream),
+               "unswizzle_scale_factors");
+  return out;
+}
+
 void py_clear_device_status() {
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   check_status(nvfp4_clear_device_status(stream), "clear_device_status");
@@ -201,6 +240,12 @@ PYBIND11_MODULE(my_plugins, m) {
   m.def("quantize_nvfp4_auto_scale", &py_quantize_nvfp4_auto_scale,
         "quantize with s = 6*448/amax computed on the device; returns (packed, sf, s)",
         py::arg("input"));
+  m.def("swizzle_scale_factors", &py_swizzle_scale_factors,
+        "scale factors [..., cols] -> the 128x4 blocked layout of library block-scaled GEMMs",
+        py::arg("sf"));
+  m.def("unswizzle_scale_factors", &py_unswizzle_scale_factors,
+        "blocked scale factors -> float8_e4m3fn [rows, cols]", py::arg("blocked"), py::arg("rows"),
+        py::arg("cols"));
   m.def("device_status", &py_device_status,
         "status word of the library's kernels on the current device (0 = OK)");
   m.def("clear_device_status", &py_clear_device_status, "reset the device status word to 0");

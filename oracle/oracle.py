@@ -175,6 +175,30 @@ def bf16_to_f32_array(h: np.ndarray) -> np.ndarray:
 
 
 # ---- the reference's own kernels, rebuilt for sm_100a (GPU box only) -----------------------
+def scale_to_blocked(sf: np.ndarray) -> np.ndarray:
+    """Row-major scale factors uint8 [rows, cols] -> the 128x4 blocked layout (1-D uint8).
+
+    Not a reference function: the reference's factors only feed its own kernel. This restates
+    the published block-scaling-factor layout of library block-scaled GEMMs (cuBLASLt; the one
+    torch._scaled_mm takes for float4_e2m1fn_x2 operands): pad rows to a multiple of 128 and
+    cols to a multiple of 4 with zeros, cut into 128x4 blocks stored row-block-major, and inside
+    a block put row 32*i + j, column c at byte 16*j + 4*i + c.
+    """
+    rows, cols = sf.shape
+    rp, cp = -(-rows // 128) * 128, -(-cols // 4) * 4
+    x = np.zeros((rp, cp), dtype=np.uint8)
+    x[:rows, :cols] = sf
+    # (row-block, i, j, col-block, c) -> (row-block, col-block, j, i, c)
+    return np.ascontiguousarray(x.reshape(rp // 128, 4, 32, cp // 4, 4).transpose(0, 3, 2, 1, 4)).reshape(-1)
+
+
+def scale_from_blocked(blocked: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Inverse of scale_to_blocked: drops the padding."""
+    rp, cp = -(-rows // 128) * 128, -(-cols // 4) * 4
+    x = blocked.reshape(rp // 128, cp // 4, 32, 4, 4).transpose(0, 3, 2, 1, 4).reshape(rp, cp)
+    return np.ascontiguousarray(x[:rows, :cols])
+
+
 def load_reference_kernels():
     """ctypes handle on oracle/_ref/libref_quantize.so, or None if it was not built."""
     if not os.path.exists(_REF_PATH):
