@@ -131,6 +131,36 @@ int nvfp4_gemm_host_scale(const void* A, const void* B, const void* A_sf, const 
                           cudaStream_t stream);
 
 /*
+ * Column-parallel GEMM with the all-gather of D fused into the epilogue (one process per GPU).
+ * The reference has no multi-GPU path; this replaces "gemm_nvfp4 on a column shard of B, then an
+ * all-gather of the shards' outputs". Every rank passes the same A, its own shard B_shard
+ * [N_local, K/2] (+ B_sf_shard [N_local, K/16]) and `outputs`: a HOST array of `world` device
+ * addresses, outputs[r] = rank r's full output D_r, bf16 [M, world * N_local] row-major, as
+ * mapped in this process (its own buffer, and peers' buffers opened with nvfp4_ipc_open). The
+ * kernel stores this rank's columns [rank*N_local, (rank+1)*N_local) of every tile into every
+ * D_r over NVLink while later tiles compute. It does not wait for the other ranks: before any
+ * rank reads D_r, every rank's call must have completed (e.g. a small all-reduce on the stream
+ * after the call), and no rank may start the next call into the same buffers before every rank
+ * has finished reading the previous result. Requires N_local % 8 == 0, world <= 8.
+ */
+int nvfp4_gemm_allgather(const void* A, const void* B_shard, const void* A_sf,
+                         const void* B_sf_shard, const float* scale, void* const* outputs,
+                         int world, int rank, int64_t M, int64_t N_local, int64_t K,
+                         cudaStream_t stream);
+
+/*
+ * Sharing a device buffer with the other processes of the node (CUDA IPC). No reference
+ * counterpart. nvfp4_ipc_export writes the IPC handle (NVFP4_IPC_HANDLE_BYTES bytes) of the
+ * allocation containing `ptr` and ptr's offset in it; another process maps it with
+ * nvfp4_ipc_open (on its current device, peer access enabled lazily) and unmaps it with
+ * nvfp4_ipc_close(ptr, offset). A process cannot open its own handles.
+ */
+#define NVFP4_IPC_HANDLE_BYTES 64
+int nvfp4_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+int nvfp4_ipc_open(const void* handle, int64_t offset, void** ptr_out);
+int nvfp4_ipc_close(void* ptr, int64_t offset);
+
+/*
  * Scale factors in the 128x4 blocked layout that library block-scaled GEMMs consume (cuBLASLt's
  * block-scaling-factor layout; torch._scaled_mm with float4_e2m1fn_x2 operands). No reference
  * counterpart: the reference's factors only feed its own kernel. Row-major sf[rows][cols]

@@ -26,7 +26,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-Wall", f"-I{INCLUDE}"] + ARCH
 
-CU_SOURCES = ["quantize.cu", "gemm_sm100.cu", "scale_layout.cu"]
+CU_SOURCES = ["quantize.cu", "gemm_sm100.cu", "scale_layout.cu", "peer.cu"]
 HEADERS = ["ptx.cuh", "capi_util.h"]
 
 LIB_NAME = "libnvfp4_b200.so"

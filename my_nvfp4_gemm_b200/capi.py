@@ -41,6 +41,10 @@ SIGNATURES = {
     "nvfp4_dequantize_host_scale": ([_P, _F32, _P, _I64, _P, _P], _INT),
     "nvfp4_gemm": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P], _INT),
     "nvfp4_gemm_host_scale": ([_P, _P, _P, _P, _F32, _P, _I64, _I64, _I64, _P], _INT),
+    "nvfp4_gemm_allgather": ([_P, _P, _P, _P, _P, ctypes.POINTER(_P), _INT, _INT, _I64, _I64, _I64, _P], _INT),
+    "nvfp4_ipc_export": ([_P, _P, ctypes.POINTER(_I64)], _INT),
+    "nvfp4_ipc_open": ([_P, _I64, ctypes.POINTER(_P)], _INT),
+    "nvfp4_ipc_close": ([_P, _I64], _INT),
     "nvfp4_blocked_scale_bytes": ([_I64, _I64], _I64),
     "nvfp4_scale_to_blocked": ([_P, _I64, _I64, _P, _P], _INT),
     "nvfp4_scale_from_blocked": ([_P, _I64, _I64, _P, _P], _INT),
@@ -123,6 +127,36 @@ def gemm(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, d_ptr, m, n, k, stream=0) ->
 
 def gemm_host_scale(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale, d_ptr, m, n, k, stream=0) -> int:
     return lib().nvfp4_gemm_host_scale(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale, d_ptr, m, n, k, stream)
+
+
+def gemm_allgather(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, output_ptrs, rank, m, n_local, k,
+                   stream=0) -> int:
+    arr = (_P * len(output_ptrs))(*output_ptrs)
+    return lib().nvfp4_gemm_allgather(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, arr, len(output_ptrs),
+                                      rank, m, n_local, k, stream)
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_export(ptr) -> tuple[bytes, int]:
+    """(handle bytes, offset) of the device allocation containing ptr."""
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    off = _I64(0)
+    check(lib().nvfp4_ipc_export(ptr, buf, ctypes.byref(off)), "nvfp4_ipc_export")
+    return buf.raw, off.value
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """Map another process's exported buffer on the current device; returns its address here."""
+    p = _P(0)
+    check(lib().nvfp4_ipc_open(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), offset,
+                               ctypes.byref(p)), "nvfp4_ipc_open")
+    return p.value
+
+
+def ipc_close(ptr, offset) -> None:
+    check(lib().nvfp4_ipc_close(ptr, offset), "nvfp4_ipc_close")
 
 
 def blocked_scale_bytes(rows, cols) -> int:

@@ -183,11 +183,22 @@ __device__ __forceinline__ void write_sf_slot(uint32_t slot, uint32_t sfa_s, uin
   ptx::tmem_st_32x32b_x16(slot + C::BN / 8, va);
 }
 
-template <class C>
+// Where the epilogue stores D: NDST = 1 for the plain GEMM; the column-parallel form with a
+// fused all-gather passes one map per rank, each covering this rank's column slice of that
+// rank's full output (so the TMA unit clips at the slice edge), local output first.
+constexpr int kMaxRanks = 8;
+
+template <int NDST>
+struct DstMaps {
+  CUtensorMap map[NDST];
+  int count;  // maps in use, 1..NDST
+};
+
+template <class C, int NDST>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
             const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
-            const __grid_constant__ CUtensorMap tm_d, const Params p) {
+            const __grid_constant__ DstMaps<NDST> dst, const Params p) {
   constexpr bool kPair = C::PAIR;
   constexpr int kGroup = C::CTAS;
   extern __shared__ uint8_t smem_raw[];
@@ -241,7 +252,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     ptx::tma_prefetch_desc(&tm_b);
     ptx::tma_prefetch_desc(&tm_sfa);
     ptx::tma_prefetch_desc(&tm_sfb);
-    ptx::tma_prefetch_desc(&tm_d);
+    for (int i = 0; i < dst.count; ++i) ptx::tma_prefetch_desc(&dst.map[i]);
   }
   if (warp == kMmaWarp) {
     ptx::tmem_alloc_g<kGroup>(tmem_slot, C::TMEM_COLS);
@@ -480,13 +491,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         // Boxes that start inside D are clipped by the TMA unit; boxes entirely outside
         // (ragged M or N) are skipped.
         if (lane == 0 && m_cta + ew * 32 < p.m && n0 + c * kEpiCols < p.n) {
-          ptx::tma_store_2d(&tm_d, buf, n0 + c * kEpiCols, m_cta + ew * 32);
+          // Peers' outputs are written over NVLink straight from this staging buffer; the tile
+          // reaches every rank while the next tile's MMAs run.
+          for (int i = 0; i < (NDST == 1 ? 1 : dst.count); ++i)
+            ptx::tma_store_2d(&dst.map[i], buf, n0 + c * kEpiCols, m_cta + ew * 32);
           ptx::bulk_commit_group();
         }
       }
       if (++acc == C::ACC_STAGES) { acc = 0; acc_phase ^= 1; }
     }
-    if (lane == 0) ptx::bulk_wait_group<0>();
+    if (lane == 0) {
+      ptx::bulk_wait_group<0>();
+      // Stores into other GPUs' memory must be visible system-wide before the kernel ends
+      // (the caller orders the ranks' reads after every rank's kernel).
+      if constexpr (NDST > 1) __threadfence_system();
+    }
   }
 
   ptx::tc_fence_before_sync();
@@ -500,13 +519,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
 }
 
 // K == 0: the sum is empty; D = bf16(0 / scale), as the reference epilogue would produce.
-__global__ void fill_empty_k_kernel(uint16_t* __restrict__ d, int64_t n, const float* scale_ptr,
-                                    float scale_val) {
+// D is rows x cols with a row pitch of ld elements.
+__global__ void fill_empty_k_kernel(uint16_t* __restrict__ d, int64_t rows, int64_t cols,
+                                    int64_t ld, const float* scale_ptr, float scale_val) {
   const float scale = scale_ptr ? __ldg(scale_ptr) : scale_val;
   const uint32_t v = ptx::f32x2_to_bf16x2(__fdiv_rn(0.0f, scale), 0.0f) & 0xFFFFu;
+  const int64_t n = rows * cols;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n;
        i += int64_t(gridDim.x) * blockDim.x)
-    d[i] = static_cast<uint16_t>(v);
+    d[(i / cols) * ld + i % cols] = static_cast<uint16_t>(v);
 }
 
 // Self-test of the bounded wait: nothing ever arrives on this barrier.
@@ -563,14 +584,14 @@ constexpr int kMaxDevices = 64;
 
 // Per device, once: raise the dynamic shared-memory limit and find how many CTAs (single) or
 // CTA pairs (clusters of 2) can be resident at once — the persistent grid size.
-template <class C>
+template <class C, int NDST>
 int resident_units(int dev) {
   static std::once_flag flags[kMaxDevices];
   static int units[kMaxDevices];
   static cudaError_t errs[kMaxDevices];
   if (dev < 0 || dev >= kMaxDevices) return -NVFP4_ERR_NO_DEVICE;
   std::call_once(flags[dev], [&] {
-    errs[dev] = cudaFuncSetAttribute(gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    errs[dev] = cudaFuncSetAttribute(gemm_kernel<C, NDST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::SMEM_ALLOC);
     if (errs[dev] != cudaSuccess) return;
     int sms = 0;
@@ -589,7 +610,7 @@ int resident_units(int dev) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int clusters = 0;
-      errs[dev] = cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<C>, &cfg);
+      errs[dev] = cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<C, NDST>, &cfg);
       units[dev] = clusters > 0 ? clusters : sms / 2;
     } else {
       units[dev] = sms;
@@ -606,16 +627,26 @@ using CfgSingle = Cfg<256, 4, 1, false, 1, 4>;
 // per shared-memory slot (64-byte rows, 2 slots); tensor memory 256 + 5 x 48 columns.
 using CfgPair = Cfg<256, 5, 1, true, 4, 2>;
 
-template <class C>
+// D of this launch: `count` destinations, each [M, N] with its own base and row pitch.
+struct DstDesc {
+  void* base[kMaxRanks];
+  uint64_t row_bytes;
+  int count;
+};
+
+template <class C, int NDST>
 int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
-           const float* scale_ptr, float scale_val, void* D, int64_t M, int64_t N, int64_t K,
-           cudaStream_t stream) {
+           const float* scale_ptr, float scale_val, const DstDesc& dd, int64_t M, int64_t N,
+           int64_t K, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NVFP4_ERR_NO_DEVICE;
-  const int units = resident_units<C>(dev);
+  const int units = resident_units<C, NDST>(dev);
   if (units <= 0) return units == 0 ? NVFP4_ERR_NO_DEVICE : -units;
+  if (dd.count < 1 || dd.count > NDST) return NVFP4_ERR_INVALID_VALUE;
 
-  CUtensorMap tm_a, tm_b, tm_sfa, tm_sfb, tm_d;
+  CUtensorMap tm_a, tm_b, tm_sfa, tm_sfb;
+  DstMaps<NDST> dst;
+  dst.count = dd.count;
   const uint64_t kb = uint64_t(K) / 2, ks = uint64_t(K) / 16;
   // Scale-factor rows of 16/32/64 bytes per slot; the wider ones swizzled (see sf_chunk_addr).
   const CUtensorMapSwizzle sf_swizzle = C::SF_ROW_BYTES == 64   ? CU_TENSOR_MAP_SWIZZLE_64B
@@ -628,9 +659,10 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
             make_map_2d(&tm_sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, A_sf, ks, M, ks, C::SF_ROW_BYTES,
                         kRowsPerCta, sf_swizzle) &&
             make_map_2d(&tm_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, B_sf, ks, N, ks, C::SF_ROW_BYTES,
-                        C::BN, sf_swizzle) &&
-            make_map_2d(&tm_d, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, D, N, M, uint64_t(N) * 2,
-                        kEpiCols, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+                        C::BN, sf_swizzle);
+  for (int i = 0; ok && i < dd.count; ++i)
+    ok = make_map_2d(&dst.map[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dd.base[i], N, M, dd.row_bytes,
+                     kEpiCols, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (!ok) return encode_fn() ? NVFP4_ERR_INVALID_VALUE : NVFP4_ERR_NO_DEVICE;
 
   Params p;
@@ -658,11 +690,11 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return status_from_cuda(cudaLaunchKernelEx(&cfg, gemm_kernel<C>, tm_a, tm_b, tm_sfa, tm_sfb,
-                                               tm_d, p));
+    return status_from_cuda(cudaLaunchKernelEx(&cfg, gemm_kernel<C, NDST>, tm_a, tm_b, tm_sfa,
+                                               tm_sfb, dst, p));
   } else {
-    gemm_kernel<C><<<grid_units, kThreads, C::SMEM_ALLOC, stream>>>(tm_a, tm_b, tm_sfa, tm_sfb,
-                                                                   tm_d, p);
+    gemm_kernel<C, NDST><<<grid_units, kThreads, C::SMEM_ALLOC, stream>>>(tm_a, tm_b, tm_sfa,
+                                                                         tm_sfb, dst, p);
     return status_from_cuda(cudaGetLastError());
   }
 }
@@ -676,17 +708,63 @@ int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const 
   if (!D) return NVFP4_ERR_INVALID_VALUE;
   if (!aligned_to(D, 16)) return NVFP4_ERR_MISALIGNED;
   if (K == 0) {
-    fill_empty_k_kernel<<<148, 256, 0, stream>>>(static_cast<uint16_t*>(D), M * N, scale_ptr,
+    fill_empty_k_kernel<<<148, 256, 0, stream>>>(static_cast<uint16_t*>(D), M, N, N, scale_ptr,
                                                  scale_val);
     return status_from_cuda(cudaGetLastError());
   }
   if (!A || !B || !A_sf || !B_sf) return NVFP4_ERR_INVALID_VALUE;
   if (!aligned_to(A, 16) || !aligned_to(B, 16) || !aligned_to(A_sf, 16) || !aligned_to(B_sf, 16))
     return NVFP4_ERR_MISALIGNED;
+  DstDesc dd = {};
+  dd.base[0] = D;
+  dd.row_bytes = uint64_t(N) * 2;
+  dd.count = 1;
   // A CTA pair covers 256 rows; for M <= 128 a single CTA per tile wastes no tensor work.
   if (M > kRowsPerCta)
-    return launch<CfgPair>(A, B, A_sf, B_sf, scale_ptr, scale_val, D, M, N, K, stream);
-  return launch<CfgSingle>(A, B, A_sf, B_sf, scale_ptr, scale_val, D, M, N, K, stream);
+    return launch<CfgPair, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+  return launch<CfgSingle, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+}
+
+// Column-parallel GEMM with the all-gather fused into the epilogue. Every rank holds the same
+// A, its own column shard of B ([N_local, K/2]) and a full output D_r [M, world * N_local];
+// `outputs[r]` is rank r's D_r as mapped in this process. This rank's tile results are stored
+// into columns [rank * N_local, (rank + 1) * N_local) of every D_r.
+int run_allgather(const void* A, const void* B, const void* A_sf, const void* B_sf,
+                  const float* scale_ptr, float scale_val, void* const* outputs, int world,
+                  int rank, int64_t M, int64_t N_local, int64_t K, cudaStream_t stream) {
+  if (M < 0 || N_local < 0 || K < 0) return NVFP4_ERR_INVALID_VALUE;
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !outputs)
+    return NVFP4_ERR_INVALID_VALUE;
+  if (K % kBK != 0 || N_local % 8 != 0) return NVFP4_ERR_UNSUPPORTED_SHAPE;
+  if (M > 0x7FFFFFFF || K > 0x7FFFFFFF || N_local * world > 0x7FFFFFFF) return NVFP4_ERR_TOO_LARGE;
+  if (M == 0 || N_local == 0) return NVFP4_OK;
+  DstDesc dd = {};
+  dd.row_bytes = uint64_t(N_local) * uint64_t(world) * 2;
+  dd.count = world;
+  for (int i = 0; i < world; ++i) {
+    const int r = (rank + i) % world;  // local output first, then the next ranks in turn
+    if (!outputs[r]) return NVFP4_ERR_INVALID_VALUE;
+    if (!aligned_to(outputs[r], 16)) return NVFP4_ERR_MISALIGNED;
+    dd.base[i] = static_cast<uint8_t*>(outputs[r]) + uint64_t(rank) * uint64_t(N_local) * 2;
+  }
+  if (K == 0) {
+    for (int i = 0; i < world; ++i) {
+      fill_empty_k_kernel<<<148, 256, 0, stream>>>(static_cast<uint16_t*>(dd.base[i]), M,
+                                                   N_local, int64_t(dd.row_bytes / 2), scale_ptr,
+                                                   scale_val);
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return status_from_cuda(e);
+    }
+    return NVFP4_OK;
+  }
+  if (!A || !B || !A_sf || !B_sf) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned_to(A, 16) || !aligned_to(B, 16) || !aligned_to(A_sf, 16) || !aligned_to(B_sf, 16))
+    return NVFP4_ERR_MISALIGNED;
+  if (M > kRowsPerCta)
+    return launch<CfgPair, kMaxRanks>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N_local, K,
+                                      stream);
+  return launch<CfgSingle, kMaxRanks>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N_local, K,
+                                      stream);
 }
 
 }  // namespace gemm
@@ -718,6 +796,15 @@ int nvfp4_gemm_host_scale(const void* A, const void* B, const void* A_sf, const 
                           float scale, void* D, int64_t M, int64_t N, int64_t K,
                           cudaStream_t stream) {
   return nvfp4::gemm::run(A, B, A_sf, B_sf, nullptr, scale, D, M, N, K, stream);
+}
+
+int nvfp4_gemm_allgather(const void* A, const void* B_shard, const void* A_sf,
+                         const void* B_sf_shard, const float* scale, void* const* outputs,
+                         int world, int rank, int64_t M, int64_t N_local, int64_t K,
+                         cudaStream_t stream) {
+  if (!scale) return NVFP4_ERR_INVALID_VALUE;
+  return nvfp4::gemm::run_allgather(A, B_shard, A_sf, B_sf_shard, scale, 0.0f, outputs, world,
+                                    rank, M, N_local, K, stream);
 }
 
 int nvfp4_device_status(int* status_out, cudaStream_t stream) {

@@ -13,8 +13,11 @@
 //     last dim % 16 (quantize), sf shape mismatches, K mismatch between A and B, K % 256 and
 //     N % 8 (the reference assert()s, gemm_nvfp4.cu:246);
 //   * sizes are 64-bit.
+#include <vector>
+
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <pybind11/stl.h>
 #include <torch/extension.h>
 
 #include "../../include/nvfp4_b200.h"
@@ -175,6 +178,52 @@ torch::Tensor py_gemm_nvfp4(const torch::Tensor& A, const torch::Tensor& B,
   return D;
 }
 
+// Extension (no reference counterpart): the column-parallel GEMM with the all-gather fused into
+// its epilogue. `output` is this rank's full D [M, world * N_local] (bf16, contiguous) and
+// `output_ptrs[r]` the address, in this process, of rank r's D (output_ptrs[rank] ==
+// output.data_ptr(); the others mapped through nvfp4_ipc_open). The caller orders the ranks:
+// every rank's call completes before any rank reads D, and no rank reuses the buffers before
+// every rank has read the previous result (my_nvfp4_gemm_b200.sharded does both).
+void py_gemm_nvfp4_allgather(const torch::Tensor& A, const torch::Tensor& B_shard,
+                             const torch::Tensor& A_sf, const torch::Tensor& B_sf_shard,
+                             const torch::Tensor& scale, const torch::Tensor& output,
+                             const std::vector<int64_t>& output_ptrs, int64_t rank) {
+  TORCH_CHECK(A.dtype() == torch::kUInt8 && A.is_contiguous() && A.dim() == 2,
+              "A must be 2D uint8 and contiguous");
+  TORCH_CHECK(B_shard.dtype() == torch::kUInt8 && B_shard.is_contiguous() && B_shard.dim() == 2,
+              "B_shard must be 2D uint8 and contiguous");
+  TORCH_CHECK(A_sf.dtype() == torch::kFloat8_e4m3fn && A_sf.is_contiguous() &&
+                  B_sf_shard.dtype() == torch::kFloat8_e4m3fn && B_sf_shard.is_contiguous(),
+              "A_sf and B_sf_shard must be float8_e4m3 and contiguous");
+  TORCH_CHECK(scale.dtype() == torch::kFloat32 && 0 == scale.dim() && scale.is_cuda(),
+              "scale must be a float32 scalar on the GPU");
+  TORCH_CHECK(A.is_cuda() && B_shard.device() == A.device() && A_sf.device() == A.device() &&
+                  B_sf_shard.device() == A.device() && scale.device() == A.device() &&
+                  output.device() == A.device(),
+              "all tensors must be on the same cuda device");
+  const int64_t world = int64_t(output_ptrs.size());
+  const int64_t M = A.size(0), N_local = B_shard.size(0), K = A.size(1) * 2;
+  TORCH_CHECK(world >= 1 && world <= 8, "1..8 ranks supported, got ", world);
+  TORCH_CHECK(rank >= 0 && rank < world, "rank out of range");
+  TORCH_CHECK(B_shard.size(1) * 2 == K, "A and B_shard must have the same K");
+  TORCH_CHECK(K % 256 == 0 && N_local % 8 == 0, "K % 256 == 0 and N_local % 8 == 0 required");
+  TORCH_CHECK(A_sf.numel() == M * (K / 16) && B_sf_shard.numel() == N_local * (K / 16),
+              "scale-factor tensors must hold [rows, K/16] factors");
+  TORCH_CHECK(output.dtype() == torch::kBFloat16 && output.is_contiguous() && output.dim() == 2 &&
+                  output.size(0) == M && output.size(1) == world * N_local,
+              "output must be bf16 [M, world * N_local] and contiguous");
+  TORCH_CHECK(output_ptrs[rank] == reinterpret_cast<int64_t>(output.data_ptr()),
+              "output_ptrs[rank] must be output's own address");
+  const c10::cuda::CUDAGuard guard(A.device());
+  std::vector<void*> ptrs(world);
+  for (int64_t r = 0; r < world; ++r) ptrs[r] = reinterpret_cast<void*>(output_ptrs[r]);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(A.device().index());
+  check_status(nvfp4_gemm_allgather(A.data_ptr(), B_shard.data_ptr(), A_sf.data_ptr(),
+                                    B_sf_shard.data_ptr(), scale.data_ptr<float>(), ptrs.data(),
+                                    int(world), int(rank), M, N_local, K, stream),
+               "gemm_nvfp4_allgather");
+}
+
 // Device status word of the library on the current CUDA device (synchronises the stream).
 int64_t py_device_status() {
   int v = 0;
@@ -240,6 +289,10 @@ PYBIND11_MODULE(my_plugins, m) {
   m.def("quantize_nvfp4_auto_scale", &py_quantize_nvfp4_auto_scale,
         "quantize with s = 6*448/amax computed on the device; returns (packed, sf, s)",
         py::arg("input"));
+  m.def("gemm_nvfp4_allgather", &py_gemm_nvfp4_allgather,
+        "column-parallel GEMM storing this rank's columns into every rank's output",
+        py::arg("A"), py::arg("B_shard"), py::arg("A_sf"), py::arg("B_sf_shard"), py::arg("scale"),
+        py::arg("output"), py::arg("output_ptrs"), py::arg("rank"));
   m.def("swizzle_scale_factors", &py_swizzle_scale_factors,
         "scale factors [..., cols] -> the 128x4 blocked layout of library block-scaled GEMMs",
         py::arg("sf"));

@@ -86,17 +86,76 @@ def quantize_row_sharded(x_local: torch.Tensor, group=None,
     return q, sf, s
 
 
+class PeerOutput:
+    """A bf16 [M, N] output buffer on every rank of `group`, each mapped into every rank's
+    process (CUDA IPC over NVLink), for the GEMM whose epilogue writes all ranks' outputs.
+
+    ``ptrs[r]`` is rank r's buffer as addressed in this process. The buffer is reused by every
+    fused call with the same shape; a call's result stays valid until the next such call."""
+
+    def __init__(self, M: int, N: int, device: torch.device, group=None):
+        from . import capi
+        self.world, self.rank = world_and_rank(group)
+        self.local = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+        handle, offset = capi.ipc_export(self.local.data_ptr())
+        shared = [None] * self.world
+        dist.all_gather_object(shared, (handle, offset), group=group)
+        self.ptrs, self._opened = [], []
+        for r, (h, off) in enumerate(shared):
+            if r == self.rank:
+                self.ptrs.append(self.local.data_ptr())
+            else:
+                p = capi.ipc_open(h, off)
+                self._opened.append((p, off))
+                self.ptrs.append(p)
+
+    def close(self) -> None:
+        from . import capi
+        torch.cuda.synchronize(self.local.device)
+        for p, off in self._opened:
+            capi.ipc_close(p, off)
+        self._opened = []
+
+
+_peer_outputs: dict = {}
+
+
+def peer_output(M: int, N: int, device: torch.device, group=None) -> PeerOutput:
+    key = (M, N, str(device), id(group))
+    po = _peer_outputs.get(key)
+    if po is None:
+        po = _peer_outputs[key] = PeerOutput(M, N, device, group)
+    return po
+
+
+def release_peer_outputs() -> None:
+    """Unmap every peer buffer (call on every rank before destroying the process group)."""
+    for po in _peer_outputs.values():
+        po.close()
+    _peer_outputs.clear()
+
+
+def _rank_barrier(device: torch.device, group=None) -> None:
+    # A one-element all-reduce on the current stream: it completes on a rank only after every
+    # rank's earlier work on its stream has completed.
+    dist.all_reduce(torch.zeros(1, device=device), group=group)
+
+
 def gemm_column_parallel(A: torch.Tensor, B_shard: torch.Tensor, A_sf: torch.Tensor,
                          B_sf_shard: torch.Tensor, scale: torch.Tensor, group=None,
                          gather: bool = False, chunks: int = 4,
-                         gemm_fn: Optional[Callable] = None) -> torch.Tensor:
+                         gemm_fn: Optional[Callable] = None, fused: bool = False) -> torch.Tensor:
     """D[:, shard] = gemm_nvfp4(A, B_shard) on this rank; with gather=True the full D [M, N]
     (all ranks' shards, rank order along N) on every rank.
 
-    The gather needs equal shard widths on all ranks (all_gather_into_tensor); it is issued per
-    chunk of M rows right after that chunk's GEMM so NCCL overlaps the next chunk's compute."""
+    gather=True, fused=False: the GEMM runs per chunk of M rows and each chunk's NCCL
+    all_gather_into_tensor overlaps the next chunk's compute. fused=True: one GEMM whose
+    epilogue stores this rank's tiles into every rank's output over NVLink (no collective for
+    the data; two one-element all-reduces order the ranks before and after). The fused result
+    is a shared buffer, valid until the next fused call of the same shape. Both need equal
+    shard widths on all ranks."""
     fn = gemm_fn or _plugins().gemm_nvfp4
-    world, _ = world_and_rank(group)
+    world, rank = world_and_rank(group)
     if not gather or world == 1:
         return fn(A, B_shard, A_sf, B_sf_shard, scale)
 
@@ -107,6 +166,13 @@ def gemm_column_parallel(A: torch.Tensor, B_shard: torch.Tensor, A_sf: torch.Ten
     if len(set(w)) != 1:
         raise ValueError(f"gather needs equal shard widths on all ranks, got {w}")
     n = w[0]
+    if fused:
+        po = peer_output(A.shape[0], world * n, A.device, group)
+        _rank_barrier(A.device, group)      # every rank is done with the previous result
+        _plugins().gemm_nvfp4_allgather(A, B_shard, A_sf, B_sf_shard, scale, po.local, po.ptrs,
+                                        rank)
+        _rank_barrier(A.device, group)      # every rank's stores have landed
+        return po.local
     M = A.shape[0]
     chunks = max(1, min(chunks, M))
     bounds = [M * i // chunks for i in range(chunks + 1)]

@@ -2,7 +2,8 @@
 
 Each rank: quantize its rows of the activation with the global scale (one all_reduce(MAX)),
 all-gather the packed activation, run the column-parallel GEMM on its weight shard with the
-chunked NCCL all-gather of D, and compare with the unsharded single-GPU result on every rank.
+chunked NCCL all-gather of D and with the all-gather fused into the GEMM epilogue (stores into
+every rank's output over NVLink), and compare with the unsharded single-GPU result on every rank.
 """
 import datetime
 import os
@@ -52,7 +53,20 @@ def main():
     assert torch.equal(local.view(torch.int16), full[:, n0:n1].view(torch.int16)), "local shard differs"
     gathered = sharded.gemm_column_parallel(x, w_sh, x_sf, w_sf_sh, sX * sW, gather=True, chunks=3)
     assert torch.equal(gathered.view(torch.int16), full.view(torch.int16)), "gathered D differs"
+
+    # the all-gather fused into the GEMM epilogue (stores into every rank's output over
+    # NVLink): bit-identical to the single-GPU result, on repeated calls into the same buffers
+    for it in range(3):
+        fused = sharded.gemm_column_parallel(x, w_sh, x_sf, w_sf_sh, sX * sW, gather=True,
+                                             fused=True)
+        assert torch.equal(fused.view(torch.int16), full.view(torch.int16)), f"fused D differs ({it})"
+    # decode-sized M (single-CTA form of the kernel) and a ragged M
+    for m in (96, 300):
+        fm = sharded.gemm_column_parallel(x[:m].contiguous(), w_sh, x_sf[:m].contiguous(), w_sf_sh,
+                                          sX * sW, gather=True, fused=True)
+        assert torch.equal(fm.view(torch.int16), full[:m].view(torch.int16)), f"fused D differs (M={m})"
     torch.cuda.synchronize()
+    sharded.release_peer_outputs()
     dist.barrier()
     dist.destroy_process_group()
     print(f"rank {rank}: ok", flush=True)
