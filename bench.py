@@ -55,6 +55,9 @@ def parse_args():
     ap.add_argument("--m", type=int, default=128, help="decode tokens (16, 32, 64, 128)")
     ap.add_argument("--gather", action="store_true",
                     help="prefill/decode: include the chunked NCCL all-gather of D in the timing")
+    ap.add_argument("--fused-gather", action="store_true",
+                    help="with --gather: the all-gather fused into the GEMM epilogue (stores into "
+                         "every rank's output over NVLink) instead of NCCL")
     return ap.parse_args()
 
 
@@ -490,9 +493,11 @@ def run_sharded_workload(args):
     stream_h = torch.cuda.current_stream().cuda_stream
     ptrs = (x.data_ptr(), w.data_ptr(), x_sf.data_ptr(), w_sf.data_ptr(), scale.data_ptr(), d.data_ptr())
 
+    fused = bool(args.gather and args.fused_gather and world > 1)
     if args.gather and world > 1:
         def step():
-            sharded.gemm_column_parallel(x, w, x_sf, w_sf, scale, gather=True, chunks=4)
+            sharded.gemm_column_parallel(x, w, x_sf, w_sf, scale, gather=True, chunks=4,
+                                         fused=fused)
     else:
         def step():
             st = capi.gemm(*ptrs, M, n_loc, K, stream_h)
@@ -517,19 +522,31 @@ def run_sharded_workload(args):
         "config": {"workload": name, "M": M, "N": N, "K": K, "n_per_rank": n_loc,
                    "parallelism": f"column-parallel N x{world}",
                    "all_gather_in_timing": bool(args.gather and world > 1),
+                   "all_gather": ("fused into the GEMM epilogue (NVLink stores)" if fused else
+                                  "NCCL all_gather_into_tensor, 4 chunks" if args.gather and world > 1
+                                  else None),
                    "l2": "flushed (256 MiB write) before every timed step"},
         "roofline": {"bound": "hbm" if M <= 128 else "tensor",
                      "achieved_tflops": achieved_tf, "frac_fp4_peak": achieved_tf / (4 * bf16_tf),
                      "achieved_gbs": achieved_gbs, "frac_hbm": achieved_gbs / hbm_gbs,
                      "algorithmic_bytes_per_rank": bytes_rank,
                      "peak_source": f"{peak_src}: HBM {hbm_gbs} GB/s, FP4 4 x bf16 {bf16_tf} TF/s"},
-        "gpu_launches": args.steps * (4 if (args.gather and world > 1) else 1),
+        "gpu_launches": args.steps * (1 if fused else 4 if (args.gather and world > 1) else 1),
         "clocks": sampler.summary(),
     }
+    if args.gather and world > 1:
+        # roofline of the GEMM with its gather: the slower of the tensor bound and this rank's
+        # output bytes over NVLink (measured 770 GB/s per direction per GPU on this pool)
+        nvlink_bytes = 2.0 * M * n_loc * (world - 1)
+        bound_ms = max(2.0 * M * n_loc * K / (4 * bf16_tf * 1e12), nvlink_bytes / 770e9) * 1e3
+        line["roofline"]["gather"] = {"nvlink_bytes_out_per_rank": nvlink_bytes,
+                                      "bound_ms": bound_ms, "frac": bound_ms / ms,
+                                      "nvlink_gbs_per_direction": 770.0}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
+        sharded.release_peer_outputs()
         dist.barrier()
         dist.destroy_process_group()
     return 0

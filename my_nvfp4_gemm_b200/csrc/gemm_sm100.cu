@@ -56,8 +56,6 @@ constexpr int kProducerWarp = 8;          // TMA producer of the A/B tiles
 constexpr int kMmaWarp = 9;               // MMA issuer, owns the TMEM allocation
 constexpr int kSfProducerWarp = 10;       // TMA producer of the scale-factor tiles
 constexpr int kThreads = 32 * 11;
-constexpr int kEpiCols = 32;              // accumulator columns per epilogue store
-constexpr int kEpiBufBytes = 32 * kEpiCols * 2;  // 32 rows x 32 bf16 per epilogue warp
 
 // Scale factors have their own shared-memory ring of SF_SLOTS slots, filled by their own
 // producer warp. One slot holds SF_KB consecutive k-blocks (16 * SF_KB bytes of every row): the
@@ -65,9 +63,22 @@ constexpr int kEpiBufBytes = 32 * kEpiCols * 2;  // 32 rows x 32 bf16 per epilog
 // 16-byte box row would fetch half of a 32-byte sector per request; 64-byte rows (SF_KB = 4)
 // use whole sectors and a quarter of the requests. Rows of 32 or 64 bytes are swizzled by the
 // TMA unit so that the writers' 16-byte reads stay free of bank conflicts.
-template <int BN_, int STAGES_, int ACC_STAGES_, bool PAIR_, int SF_KB_, int SF_SLOTS_>
+//
+// EPI_COLS: output columns per epilogue store box (32 rows x EPI_COLS bf16 staged in shared
+// memory per warp): 64 gives 128-byte rows (128B-swizzled), which is what TMA stores into
+// another GPU's memory over NVLink need to run near link rate (~666 GB/s measured, against
+// ~440 GB/s with 64-byte rows); 32 halves the staging memory.
+// EPI_BUFS: staging buffers per epilogue warp (a warp fills one while the TMA unit reads the
+// other).
+template <int BN_, int STAGES_, int ACC_STAGES_, bool PAIR_, int SF_KB_, int SF_SLOTS_,
+          int EPI_COLS_ = 32, int EPI_BUFS_ = 1>
 struct Cfg {
   static constexpr int BN = BN_;
+  static constexpr int EPI_COLS = EPI_COLS_;
+  static constexpr int EPI_BUFS = EPI_BUFS_;
+  static constexpr int EPI_ROW_BYTES = EPI_COLS * 2;
+  static constexpr int EPI_BUF_BYTES = 32 * EPI_ROW_BYTES;
+  static_assert(EPI_COLS == 32 || EPI_COLS == 64, "EPI_COLS must be 32 or 64");
   static constexpr int STAGES = STAGES_;
   static constexpr int ACC_STAGES = ACC_STAGES_;
   static constexpr bool PAIR = PAIR_;
@@ -92,7 +103,7 @@ struct Cfg {
   static constexpr int OFF_SFA = OFF_B + STAGES * B_STAGE;
   static constexpr int OFF_SFB = OFF_SFA + SF_SLOTS * SFA_SLOT;
   static constexpr int OFF_EPI = OFF_SFB + SF_SLOTS * SFB_SLOT;
-  static constexpr int OFF_BAR = OFF_EPI + kNumEpiWarps * kEpiBufBytes;
+  static constexpr int OFF_BAR = OFF_EPI + kNumEpiWarps * EPI_BUFS * EPI_BUF_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 2 * SF_SLOTS + 2 * ACC_STAGES + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16;
@@ -438,9 +449,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     const int ew = warp - kFirstEpiWarp;  // == warp % 4: TMEM lanes 32*ew .. 32*ew+31
     const float scale = p.scale_ptr ? __ldg(p.scale_ptr) : p.scale_val;
     const float alpha = __frcp_rn(scale);
-    uint8_t* buf = sEPI + ew * kEpiBufBytes;
+    uint8_t* buf = sEPI + ew * C::EPI_BUFS * C::EPI_BUF_BYTES;
     const uint32_t buf_s = ptx::smem_u32(buf);
-    const uint32_t swz = uint32_t((lane >> 1) & 3);  // 64-byte TMA swizzle of row `lane`
+    // TMA swizzle of staging row `lane`: the 16-byte chunk index XOR address bits 7.. of the row
+    const uint32_t swz = C::EPI_COLS == 64 ? uint32_t(lane & 7) : uint32_t((lane >> 1) & 3);
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
@@ -476,25 +488,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         if constexpr (kPair) ptx::mbar_arrive_cta(&tempty_bar[acc], 0);
         else ptx::mbar_arrive(&tempty_bar[acc]);
       }
+      if (lane == 0) ptx::bulk_wait_group_read<0>();  // the previous tile's stores have read
 #pragma unroll
-      for (int c = 0; c < C::BN / kEpiCols; ++c) {
-        if (lane == 0) ptx::bulk_wait_group_read<0>();  // previous store has read the buffer
+      for (int c = 0; c < C::BN / C::EPI_COLS; ++c) {
+        // Boxes entirely outside D (ragged M or N) end the loop — the issued store groups stay a
+        // prefix, which the buffer-reuse wait below counts on; boxes that start inside D are
+        // clipped by the TMA unit.
+        if (m_cta + ew * 32 >= p.m || n0 + c * C::EPI_COLS >= p.n) break;
+        const int b = c % C::EPI_BUFS;
+        if (c >= C::EPI_BUFS && lane == 0)
+          ptx::bulk_wait_group_read<C::EPI_BUFS - 1>();  // buffer b's previous store has read it
         __syncwarp();
-        const uint32_t row = buf_s + uint32_t(lane) * 64;
+        const uint32_t row =
+            buf_s + uint32_t(b * C::EPI_BUF_BYTES) + uint32_t(lane) * C::EPI_ROW_BYTES;
+        constexpr int kPairsPerChunk = C::EPI_COLS / 2;  // bf16 pairs of this row in the box
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
+        for (int k = 0; k < C::EPI_COLS / 8; ++k) {
+          const int j = c * kPairsPerChunk + 4 * k;
           ptx::st_shared_v4(row + ((uint32_t(k) ^ swz) << 4),
-                            make_uint4(pk[c * 16 + 4 * k], pk[c * 16 + 4 * k + 1],
-                                       pk[c * 16 + 4 * k + 2], pk[c * 16 + 4 * k + 3]));
+                            make_uint4(pk[j], pk[j + 1], pk[j + 2], pk[j + 3]));
+        }
         ptx::fence_proxy_async_smem();
         __syncwarp();
-        // Boxes that start inside D are clipped by the TMA unit; boxes entirely outside
-        // (ragged M or N) are skipped.
-        if (lane == 0 && m_cta + ew * 32 < p.m && n0 + c * kEpiCols < p.n) {
+        if (lane == 0) {
           // Peers' outputs are written over NVLink straight from this staging buffer; the tile
           // reaches every rank while the next tile's MMAs run.
           for (int i = 0; i < (NDST == 1 ? 1 : dst.count); ++i)
-            ptx::tma_store_2d(&dst.map[i], buf, n0 + c * kEpiCols, m_cta + ew * 32);
+            ptx::tma_store_2d(&dst.map[i], buf + b * C::EPI_BUF_BYTES, n0 + c * C::EPI_COLS,
+                              m_cta + ew * 32);
           ptx::bulk_commit_group();
         }
       }
@@ -624,8 +645,9 @@ int resident_units(int dev) {
 // (4 slots).
 using CfgSingle = Cfg<256, 4, 1, false, 1, 4>;
 // 256 x 256 tiles, CTA pair: 5-stage A/B ring per CTA (160 KiB), scale factors four k-blocks
-// per shared-memory slot (64-byte rows, 2 slots); tensor memory 256 + 5 x 48 columns.
-using CfgPair = Cfg<256, 5, 1, true, 4, 2>;
+// per shared-memory slot (64-byte rows, 2 slots), one 32 x 64 staging box per epilogue warp;
+// tensor memory 256 + 5 x 48 columns.
+using CfgPair = Cfg<256, 5, 1, true, 4, 2, 64, 1>;
 
 // D of this launch: `count` destinations, each [M, N] with its own base and row pitch.
 struct DstDesc {
@@ -662,7 +684,8 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
                         C::BN, sf_swizzle);
   for (int i = 0; ok && i < dd.count; ++i)
     ok = make_map_2d(&dst.map[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dd.base[i], N, M, dd.row_bytes,
-                     kEpiCols, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+                     C::EPI_COLS, 32,
+                     C::EPI_COLS == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   if (!ok) return encode_fn() ? NVFP4_ERR_INVALID_VALUE : NVFP4_ERR_NO_DEVICE;
 
   Params p;
