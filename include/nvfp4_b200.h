@@ -131,6 +131,19 @@ int nvfp4_gemm_host_scale(const void* A, const void* B, const void* A_sf, const 
                           cudaStream_t stream);
 
 /*
+ * GEMM whose output is quantized to NVFP4 in the epilogue, for a layer whose consumer takes
+ * NVFP4 input. No reference counterpart: it replaces nvfp4_gemm followed by nvfp4_quantize of
+ * its bf16 output and produces exactly those bytes, q_out = packed E2M1 [M, N/2] and
+ * sf_out = UE4M3 [M, N/16] of quantize(bf16(A.B^T / *scale), *out_scale), without writing or
+ * re-reading bf16 D. `scale` and `out_scale` are device pointers to fp32 values. Requires
+ * K % 256 == 0, K > 0, N % 32 == 0 (rows of q_out a multiple of 16 bytes); q_out 16-byte
+ * aligned.
+ */
+int nvfp4_gemm_quantized(const void* A, const void* B, const void* A_sf, const void* B_sf,
+                         const float* scale, const float* out_scale, void* q_out, void* sf_out,
+                         int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+
+/*
  * Column-parallel GEMM with the all-gather of D fused into the epilogue (one process per GPU).
  * The reference has no multi-GPU path; this replaces "gemm_nvfp4 on a column shard of B, then an
  * all-gather of the shards' outputs". Every rank passes the same A, its own shard B_shard

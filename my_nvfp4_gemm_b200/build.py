@@ -27,7 +27,7 @@ NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "--expt-relaxed-constexpr", "-Xc
               "-Xcompiler", "-Wall", f"-I{INCLUDE}"] + ARCH
 
 CU_SOURCES = ["quantize.cu", "gemm_sm100.cu", "scale_layout.cu", "peer.cu"]
-HEADERS = ["ptx.cuh", "capi_util.h"]
+HEADERS = ["ptx.cuh", "capi_util.h", "block_quant.cuh"]
 
 LIB_NAME = "libnvfp4_b200.so"
 EXT_NAME = "my_plugins"

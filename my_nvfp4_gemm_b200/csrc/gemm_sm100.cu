@@ -34,6 +34,7 @@
 #include <cstdint>
 #include <mutex>
 
+#include "block_quant.cuh"
 #include "capi_util.h"
 #include "ptx.cuh"
 
@@ -131,6 +132,11 @@ struct Params {
   int n_blocks;            // tiles along N (BN columns each)
   int k_stages;
   uint64_t timeout_ns;
+  // quantized output (QOUT): D is quantized to NVFP4 with the per-tensor scale *out_scale_ptr;
+  // the codes go through the destination map, the scale bytes to sf_out [m][sf_pitch].
+  const float* out_scale_ptr;
+  uint8_t* sf_out;
+  int64_t sf_pitch;
 };
 
 // Tile order: the M x N tile grid is walked in bands of kGroupM tile rows, column by column
@@ -205,7 +211,9 @@ struct DstMaps {
   int count;  // maps in use, 1..NDST
 };
 
-template <class C, int NDST>
+// QOUT: the epilogue quantizes each finished bf16 row to NVFP4 (block_quant.cuh, the same
+// arithmetic as quantize_kernel) and stores codes and scale bytes instead of bf16 D.
+template <class C, int NDST, bool QOUT = false>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
             const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
@@ -489,6 +497,46 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         else ptx::mbar_arrive(&tempty_bar[acc]);
       }
       if (lane == 0) ptx::bulk_wait_group_read<0>();  // the previous tile's stores have read
+      if constexpr (QOUT) {
+        // Codes: 128 bytes of this row per tile, staged EPI_ROW_BYTES at a time (each 16-byte
+        // chunk = two 16-column blocks); the row's 16 scale bytes go straight to sf_out.
+        const float s_out = __ldg(p.out_scale_ptr);
+        const float rcp_s_out = __frcp_rn(s_out);
+        constexpr int kColsPerChunk = C::EPI_ROW_BYTES * 2;
+        uint32_t sfw[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int c = 0; c < C::BN / kColsPerChunk; ++c) {
+          if (m_cta + ew * 32 >= p.m || n0 + c * kColsPerChunk >= p.n) break;
+          if (c >= 1 && lane == 0) ptx::bulk_wait_group_read<0>();
+          __syncwarp();
+          const uint32_t row = buf_s + uint32_t(lane) * C::EPI_ROW_BYTES;
+#pragma unroll
+          for (int k = 0; k < C::EPI_ROW_BYTES / 16; ++k) {
+            const int blk = c * (kColsPerChunk / 16) + 2 * k;  // first of the two blocks
+            uint32_t lo0, hi0, lo1, hi1;
+            const uint8_t s0 = bq::quantize_block16(&pk[blk * 8], s_out, rcp_s_out, lo0, hi0);
+            const uint8_t s1 = bq::quantize_block16(&pk[blk * 8 + 8], s_out, rcp_s_out, lo1, hi1);
+            sfw[blk / 4] |= (uint32_t(s0) | (uint32_t(s1) << 8)) << (8 * (blk % 4));
+            ptx::st_shared_v4(row + ((uint32_t(k) ^ swz) << 4), make_uint4(lo0, hi0, lo1, hi1));
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tma_store_2d(&dst.map[0], buf, (n0 + c * kColsPerChunk) / 2, m_cta + ew * 32);
+            ptx::bulk_commit_group();
+          }
+        }
+        const int r = m_cta + ew * 32 + lane;
+        const int nblk = min(16, (p.n - n0) / 16);  // scale bytes of this row inside D
+        if (r < p.m && nblk > 0) {
+          uint8_t* dst_sf = p.sf_out + int64_t(r) * p.sf_pitch + n0 / 16;
+          if (nblk == 16 && (reinterpret_cast<uintptr_t>(dst_sf) & 15) == 0) {
+            *reinterpret_cast<uint4*>(dst_sf) = make_uint4(sfw[0], sfw[1], sfw[2], sfw[3]);
+          } else {
+            for (int i = 0; i < nblk; ++i) dst_sf[i] = uint8_t(sfw[i / 4] >> (8 * (i % 4)));
+          }
+        }
+      } else {
 #pragma unroll
       for (int c = 0; c < C::BN / C::EPI_COLS; ++c) {
         // Boxes entirely outside D (ragged M or N) end the loop — the issued store groups stay a
@@ -518,6 +566,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
                               m_cta + ew * 32);
           ptx::bulk_commit_group();
         }
+      }
       }
       if (++acc == C::ACC_STAGES) { acc = 0; acc_phase ^= 1; }
     }
@@ -605,14 +654,14 @@ constexpr int kMaxDevices = 64;
 
 // Per device, once: raise the dynamic shared-memory limit and find how many CTAs (single) or
 // CTA pairs (clusters of 2) can be resident at once — the persistent grid size.
-template <class C, int NDST>
+template <class C, int NDST, bool QOUT>
 int resident_units(int dev) {
   static std::once_flag flags[kMaxDevices];
   static int units[kMaxDevices];
   static cudaError_t errs[kMaxDevices];
   if (dev < 0 || dev >= kMaxDevices) return -NVFP4_ERR_NO_DEVICE;
   std::call_once(flags[dev], [&] {
-    errs[dev] = cudaFuncSetAttribute(gemm_kernel<C, NDST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    errs[dev] = cudaFuncSetAttribute(gemm_kernel<C, NDST, QOUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::SMEM_ALLOC);
     if (errs[dev] != cudaSuccess) return;
     int sms = 0;
@@ -631,7 +680,7 @@ int resident_units(int dev) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int clusters = 0;
-      errs[dev] = cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<C, NDST>, &cfg);
+      errs[dev] = cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<C, NDST, QOUT>, &cfg);
       units[dev] = clusters > 0 ? clusters : sms / 2;
     } else {
       units[dev] = sms;
@@ -656,13 +705,20 @@ struct DstDesc {
   int count;
 };
 
-template <class C, int NDST>
+// Quantized output of a launch (QOUT): per-tensor scale, scale-byte destination and pitch.
+struct QOutDesc {
+  const float* out_scale = nullptr;
+  uint8_t* sf = nullptr;
+  int64_t sf_pitch = 0;
+};
+
+template <class C, int NDST, bool QOUT = false>
 int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
            const float* scale_ptr, float scale_val, const DstDesc& dd, int64_t M, int64_t N,
-           int64_t K, cudaStream_t stream) {
+           int64_t K, cudaStream_t stream, const QOutDesc& qd = QOutDesc()) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NVFP4_ERR_NO_DEVICE;
-  const int units = resident_units<C, NDST>(dev);
+  const int units = resident_units<C, NDST, QOUT>(dev);
   if (units <= 0) return units == 0 ? NVFP4_ERR_NO_DEVICE : -units;
   if (dd.count < 1 || dd.count > NDST) return NVFP4_ERR_INVALID_VALUE;
 
@@ -682,10 +738,16 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
                         kRowsPerCta, sf_swizzle) &&
             make_map_2d(&tm_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, B_sf, ks, N, ks, C::SF_ROW_BYTES,
                         C::BN, sf_swizzle);
-  for (int i = 0; ok && i < dd.count; ++i)
-    ok = make_map_2d(&dst.map[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dd.base[i], N, M, dd.row_bytes,
-                     C::EPI_COLS, 32,
-                     C::EPI_COLS == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  const CUtensorMapSwizzle epi_swizzle =
+      C::EPI_ROW_BYTES == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  for (int i = 0; ok && i < dd.count; ++i) {
+    if constexpr (QOUT)  // packed codes [M, N/2]
+      ok = make_map_2d(&dst.map[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, dd.base[i], uint64_t(N) / 2, M,
+                       dd.row_bytes, C::EPI_ROW_BYTES, 32, epi_swizzle);
+    else
+      ok = make_map_2d(&dst.map[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dd.base[i], N, M,
+                       dd.row_bytes, C::EPI_COLS, 32, epi_swizzle);
+  }
   if (!ok) return encode_fn() ? NVFP4_ERR_INVALID_VALUE : NVFP4_ERR_NO_DEVICE;
 
   Params p;
@@ -697,6 +759,9 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
   p.n_blocks = int((N + C::BN - 1) / C::BN);
   p.k_stages = int(K / kBK);
   p.timeout_ns = 2000000000ull;  // 2 s per wait: far above any legitimate stall
+  p.out_scale_ptr = qd.out_scale;
+  p.sf_out = qd.sf;
+  p.sf_pitch = qd.sf_pitch;
   const int64_t tiles = int64_t(p.m_blocks) * p.n_blocks;
   if (tiles > 0x7FFFFFFF / 2) return NVFP4_ERR_TOO_LARGE;
   const int grid_units = int(tiles < units ? tiles : units);
@@ -713,10 +778,10 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return status_from_cuda(cudaLaunchKernelEx(&cfg, gemm_kernel<C, NDST>, tm_a, tm_b, tm_sfa,
+    return status_from_cuda(cudaLaunchKernelEx(&cfg, gemm_kernel<C, NDST, QOUT>, tm_a, tm_b, tm_sfa,
                                                tm_sfb, dst, p));
   } else {
-    gemm_kernel<C, NDST><<<grid_units, kThreads, C::SMEM_ALLOC, stream>>>(tm_a, tm_b, tm_sfa,
+    gemm_kernel<C, NDST, QOUT><<<grid_units, kThreads, C::SMEM_ALLOC, stream>>>(tm_a, tm_b, tm_sfa,
                                                                          tm_sfb, dst, p);
     return status_from_cuda(cudaGetLastError());
   }
@@ -790,6 +855,34 @@ int run_allgather(const void* A, const void* B, const void* A_sf, const void* B_
                                       stream);
 }
 
+// GEMM with the output quantized to NVFP4 in the epilogue: the bytes of
+// quantize(bf16(A.B^T / scale), out_scale) without writing or re-reading bf16 D.
+int run_quantized(const void* A, const void* B, const void* A_sf, const void* B_sf,
+                  const float* scale_ptr, const float* out_scale, void* q_out, void* sf_out,
+                  int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return NVFP4_ERR_INVALID_VALUE;
+  // N % 32: the packed output's rows (N/2 bytes) must be a multiple of 16 bytes for TMA stores
+  if (K % kBK != 0 || N % 32 != 0 || K == 0) return NVFP4_ERR_UNSUPPORTED_SHAPE;
+  if (M > 0x7FFFFFFF || N > 0x7FFFFFFF || K > 0x7FFFFFFF) return NVFP4_ERR_TOO_LARGE;
+  if (M == 0 || N == 0) return NVFP4_OK;
+  if (!A || !B || !A_sf || !B_sf || !scale_ptr || !out_scale || !q_out || !sf_out)
+    return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned_to(A, 16) || !aligned_to(B, 16) || !aligned_to(A_sf, 16) || !aligned_to(B_sf, 16) ||
+      !aligned_to(q_out, 16))
+    return NVFP4_ERR_MISALIGNED;
+  DstDesc dd = {};
+  dd.base[0] = q_out;
+  dd.row_bytes = uint64_t(N) / 2;
+  dd.count = 1;
+  QOutDesc qd;
+  qd.out_scale = out_scale;
+  qd.sf = static_cast<uint8_t*>(sf_out);
+  qd.sf_pitch = N / 16;
+  if (M > kRowsPerCta)
+    return launch<CfgPair, 1, true>(A, B, A_sf, B_sf, scale_ptr, 0.0f, dd, M, N, K, stream, qd);
+  return launch<CfgSingle, 1, true>(A, B, A_sf, B_sf, scale_ptr, 0.0f, dd, M, N, K, stream, qd);
+}
+
 }  // namespace gemm
 
 int current_device_sm_count(int* device_out) {
@@ -819,6 +912,13 @@ int nvfp4_gemm_host_scale(const void* A, const void* B, const void* A_sf, const 
                           float scale, void* D, int64_t M, int64_t N, int64_t K,
                           cudaStream_t stream) {
   return nvfp4::gemm::run(A, B, A_sf, B_sf, nullptr, scale, D, M, N, K, stream);
+}
+
+int nvfp4_gemm_quantized(const void* A, const void* B, const void* A_sf, const void* B_sf,
+                         const float* scale, const float* out_scale, void* q_out, void* sf_out,
+                         int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  return nvfp4::gemm::run_quantized(A, B, A_sf, B_sf, scale, out_scale, q_out, sf_out, M, N, K,
+                                    stream);
 }
 
 int nvfp4_gemm_allgather(const void* A, const void* B_shard, const void* A_sf,

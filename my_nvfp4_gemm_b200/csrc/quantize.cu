@@ -15,6 +15,7 @@
 #include <cstdint>
 #include <mutex>
 
+#include "block_quant.cuh"
 #include "capi_util.h"
 #include "ptx.cuh"
 
@@ -24,23 +25,6 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;                                 // half-blocks per thread
 constexpr int64_t kHalfBlocksPerCta = int64_t(kThreads) * kUnroll;
-constexpr float kRcpE2m1Max = 1.0f / 6.0f;                 // 0.16666667f, as the reference
-
-__device__ __forceinline__ float bf16lo_to_f32(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16hi_to_f32(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-
-__device__ __forceinline__ uint32_t abs_max_bf16x2(uint32_t acc, uint32_t w) {
-  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&acc);
-  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&w);
-  __nv_bfloat162 r = __hmax2_nan(a, __habs2(b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-__device__ __forceinline__ uint32_t max_bf16x2(uint32_t acc, uint32_t w) {
-  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&acc);
-  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&w);
-  __nv_bfloat162 r = __hmax2_nan(a, b);
-  return *reinterpret_cast<uint32_t*>(&r);
-}
 
 // One thread = one half-block of 8 bf16. Lanes 2j and 2j+1 hold the two halves of a block.
 // kReverse: CTA b processes the chunk of CTA (grid-1-b). Used after a forward pass over the same
@@ -64,24 +48,15 @@ quantize_kernel(const uint4* __restrict__ x, const float* __restrict__ scale_ptr
 #pragma unroll
   for (int u = 0; u < kUnroll; ++u) {
     const int64_t h = base + int64_t(u) * kThreads;
-    uint32_t m = 0x00010001u;  // bf16x2 {0x0001, 0x0001}: the reference's non-zero floor
-    m = abs_max_bf16x2(m, v[u].x);
-    m = abs_max_bf16x2(m, v[u].y);
-    m = abs_max_bf16x2(m, v[u].z);
-    m = abs_max_bf16x2(m, v[u].w);
-    m = max_bf16x2(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));  // other half of the block
-    const __nv_bfloat162 m2 = *reinterpret_cast<__nv_bfloat162*>(&m);
-    const float amax = __bfloat162float(__hmax_nan(m2.x, m2.y));
-
-    const float t = __fmul_rn(__fmul_rn(amax, s), kRcpE2m1Max);
-    const uint8_t sfb = static_cast<uint8_t>(ptx::f32x2_to_e4m3x2(t, 0.0f) & 0xFFu);
-    const float os = __frcp_rn(__fmul_rn(ptx::e4m3_to_f32(sfb), rcp_s));
-
-    const uint32_t packed = ptx::f32x8_to_e2m1x8(
-        __fmul_rn(bf16lo_to_f32(v[u].x), os), __fmul_rn(bf16hi_to_f32(v[u].x), os),
-        __fmul_rn(bf16lo_to_f32(v[u].y), os), __fmul_rn(bf16hi_to_f32(v[u].y), os),
-        __fmul_rn(bf16lo_to_f32(v[u].z), os), __fmul_rn(bf16hi_to_f32(v[u].z), os),
-        __fmul_rn(bf16lo_to_f32(v[u].w), os), __fmul_rn(bf16hi_to_f32(v[u].w), os));
+    uint32_t m = bq::kAmaxSeed;
+    m = bq::abs_max_bf16x2(m, v[u].x);
+    m = bq::abs_max_bf16x2(m, v[u].y);
+    m = bq::abs_max_bf16x2(m, v[u].z);
+    m = bq::abs_max_bf16x2(m, v[u].w);
+    m = bq::max_bf16x2(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));  // other half of the block
+    float os;
+    const uint8_t sfb = bq::block_scale(bq::block_amax(m), s, rcp_s, os);
+    const uint32_t packed = bq::encode8(v[u].x, v[u].y, v[u].z, v[u].w, os);
     if (h < n_half_blocks) {
       q[h] = packed;
       if ((h & 1) == 0) sf[h >> 1] = sfb;

@@ -178,6 +178,44 @@ torch::Tensor py_gemm_nvfp4(const torch::Tensor& A, const torch::Tensor& B,
   return D;
 }
 
+// Extension (no reference counterpart): GEMM with the output quantized to NVFP4 in its
+// epilogue; the same bytes as quantize_nvfp4(gemm_nvfp4(A, B, A_sf, B_sf, scale), out_scale).
+// Both scales must be float32 scalars on the GPU. Returns (uint8 [M, N/2], float8_e4m3fn
+// [M, N/16]).
+std::tuple<torch::Tensor, torch::Tensor> py_gemm_nvfp4_quantized(
+    const torch::Tensor& A, const torch::Tensor& B, const torch::Tensor& A_sf,
+    const torch::Tensor& B_sf, const torch::Tensor& scale, const torch::Tensor& out_scale) {
+  TORCH_CHECK(A.dtype() == torch::kUInt8 && A.is_contiguous() && A.dim() == 2 &&
+                  B.dtype() == torch::kUInt8 && B.is_contiguous() && B.dim() == 2,
+              "A and B must be 2D uint8 and contiguous");
+  TORCH_CHECK(A_sf.dtype() == torch::kFloat8_e4m3fn && A_sf.is_contiguous() &&
+                  B_sf.dtype() == torch::kFloat8_e4m3fn && B_sf.is_contiguous(),
+              "A_sf and B_sf must be float8_e4m3 and contiguous");
+  for (const torch::Tensor* t : {&scale, &out_scale})
+    TORCH_CHECK(t->dtype() == torch::kFloat32 && 0 == t->dim() && t->is_cuda(),
+                "scale and out_scale must be float32 scalars on the GPU");
+  TORCH_CHECK(A.is_cuda() && B.device() == A.device() && A_sf.device() == A.device() &&
+                  B_sf.device() == A.device() && scale.device() == A.device() &&
+                  out_scale.device() == A.device(),
+              "all tensors must be on the same cuda device");
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1) * 2;
+  TORCH_CHECK(B.size(1) * 2 == K, "A and B must have the same K");
+  TORCH_CHECK(K % 256 == 0 && K > 0, "K must be a positive multiple of 256, got ", K);
+  TORCH_CHECK(N % 32 == 0, "N must be a multiple of 32 for the quantized output, got ", N);
+  TORCH_CHECK(A_sf.numel() == M * (K / 16) && B_sf.numel() == N * (K / 16),
+              "scale-factor tensors must hold [rows, K/16] factors");
+  const c10::cuda::CUDAGuard guard(A.device());
+  auto opts = torch::TensorOptions().device(A.device());
+  auto q = torch::empty({M, N / 2}, opts.dtype(torch::kUInt8));
+  auto sf = torch::empty({M, N / 16}, opts.dtype(torch::kFloat8_e4m3fn));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(A.device().index());
+  check_status(nvfp4_gemm_quantized(A.data_ptr(), B.data_ptr(), A_sf.data_ptr(), B_sf.data_ptr(),
+                                    scale.data_ptr<float>(), out_scale.data_ptr<float>(),
+                                    q.data_ptr(), sf.data_ptr(), M, N, K, stream),
+               "gemm_nvfp4_quantized");
+  return std::make_tuple(q, sf);
+}
+
 // Extension (no reference counterpart): the column-parallel GEMM with the all-gather fused into
 // its epilogue. `output` is this rank's full D [M, world * N_local] (bf16, contiguous) and
 // `output_ptrs[r]` the address, in this process, of rank r's D (output_ptrs[rank] ==
@@ -289,6 +327,10 @@ PYBIND11_MODULE(my_plugins, m) {
   m.def("quantize_nvfp4_auto_scale", &py_quantize_nvfp4_auto_scale,
         "quantize with s = 6*448/amax computed on the device; returns (packed, sf, s)",
         py::arg("input"));
+  m.def("gemm_nvfp4_quantized", &py_gemm_nvfp4_quantized,
+        "GEMM with the output quantized to NVFP4 in the epilogue; returns (packed, sf)",
+        py::arg("A"), py::arg("B"), py::arg("A_sf"), py::arg("B_sf"), py::arg("scale"),
+        py::arg("out_scale"));
   m.def("gemm_nvfp4_allgather", &py_gemm_nvfp4_allgather,
         "column-parallel GEMM storing this rank's columns into every rank's output",
         py::arg("A"), py::arg("B_shard"), py::arg("A_sf"), py::arg("B_sf_shard"), py::arg("scale"),

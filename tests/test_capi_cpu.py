@@ -91,6 +91,24 @@ def test_gemm_validation():
         capi.NVFP4_ERR_UNSUPPORTED_SHAPE
 
 
+def test_gemm_quantized_validation():
+    g = capi.gemm_quantized
+    assert g(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 128, 48, 256) == capi.NVFP4_ERR_UNSUPPORTED_SHAPE
+    assert g(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 128, 32, 0) == capi.NVFP4_ERR_UNSUPPORTED_SHAPE
+    assert g(FAKE, FAKE, FAKE, FAKE, FAKE, None, FAKE, FAKE, 128, 32, 256) == capi.NVFP4_ERR_INVALID_VALUE
+    assert g(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE + 8, FAKE, 128, 32, 256) == capi.NVFP4_ERR_MISALIGNED
+    assert g(None, None, None, None, None, None, None, None, 0, 32, 256) == capi.NVFP4_OK  # M == 0
+
+
+def test_gemm_allgather_validation():
+    g = capi.gemm_allgather
+    assert g(FAKE, FAKE, FAKE, FAKE, FAKE, [FAKE, FAKE], 2, 128, 32, 256) == capi.NVFP4_ERR_INVALID_VALUE
+    assert g(FAKE, FAKE, FAKE, FAKE, FAKE, [FAKE] * 9, 0, 128, 32, 256) == capi.NVFP4_ERR_INVALID_VALUE
+    assert g(FAKE, FAKE, FAKE, FAKE, FAKE, [FAKE, FAKE], 0, 128, 12, 256) == capi.NVFP4_ERR_UNSUPPORTED_SHAPE
+    assert g(FAKE, FAKE, FAKE, FAKE, FAKE, [FAKE, None], 0, 128, 32, 256) == capi.NVFP4_ERR_INVALID_VALUE
+    assert g(FAKE, FAKE, FAKE, FAKE, FAKE, [FAKE, FAKE + 8], 0, 128, 32, 256) == capi.NVFP4_ERR_MISALIGNED
+
+
 def test_status_out_pointer_checked():
     assert capi.lib().nvfp4_device_status(None, None) == capi.NVFP4_ERR_INVALID_VALUE
 
