@@ -412,6 +412,35 @@ def run_ours(args):
             line["gpu_launches"] += args.steps * (3 if name == "quantize_auto_scale" else 1)
         del X, y, q, qsf
 
+    # ---- NVFP4 output straight from the GEMM epilogue vs GEMM, then quantize of bf16 D
+    if not args.no_quant:
+        gemm_once()
+        s_d = (6 * 448 / d.abs().max().to(torch.float32)).reshape(())
+        qd = torch.empty(M, N // 2, dtype=torch.uint8, device="cuda")
+        qd_sf = torch.empty(M, N // 16, dtype=torch.uint8, device="cuda")
+
+        def gemm_quantized_once():
+            capi.check(capi.gemm_quantized(a.data_ptr(), b.data_ptr(), a_sf.data_ptr(),
+                                           b_sf.data_ptr(), scale.data_ptr(), s_d.data_ptr(),
+                                           qd.data_ptr(), qd_sf.data_ptr(), M, N, K, stream_h),
+                       "nvfp4_gemm_quantized")
+
+        def gemm_then_quantize():
+            gemm_once()
+            capi.check(capi.quantize(d.data_ptr(), s_d.data_ptr(), d.numel(), qd.data_ptr(),
+                                     qd_sf.data_ptr(), stream_h), "nvfp4_quantize")
+
+        n_q = max(3, min(args.steps, 100))
+        t_fused = time_device(torch, gemm_quantized_once, n_q, args.warmup, flush, world) / n_q
+        t_split = time_device(torch, gemm_then_quantize, n_q, args.warmup, flush, world) / n_q
+        line["gemm_quantized_output"] = {
+            "value": world * flops / (t_fused * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_call": t_fused, "gemm_then_quantize_ms": t_split, "steps": n_q,
+            "api": "nvfp4_gemm_quantized: NVFP4 D (bytes of quantize(bf16 D, s_out)) from the "
+                   "epilogue; compared with nvfp4_gemm + nvfp4_quantize of the bf16 D"}
+        line["gpu_launches"] += n_q * 3
+        del qd, qd_sf
+
     # ---- end to end through the torch module with pinned host buffers
     if not args.no_e2e:
         ha = a.cpu().pin_memory()

@@ -62,16 +62,55 @@ __device__ __forceinline__ uint32_t encode8(uint32_t w0, uint32_t w1, uint32_t w
                               __fmul_rn(bf16lo_to_f32(w3), os), __fmul_rn(bf16hi_to_f32(w3), os));
 }
 
-// A whole block held by one thread: 16 bf16 in w[0..7] -> 8 code bytes (lo, hi words) + scale.
-__device__ __forceinline__ uint8_t quantize_block16(const uint32_t* w, float s, float rcp_s,
+// A whole block held by one thread: 16 bf16 in w0..w7 (by value, so callers' arrays stay in
+// registers) -> 8 code bytes (lo, hi words) + scale byte.
+__device__ __forceinline__ uint8_t quantize_block16(uint32_t w0, uint32_t w1, uint32_t w2,
+                                                    uint32_t w3, uint32_t w4, uint32_t w5,
+                                                    uint32_t w6, uint32_t w7, float s, float rcp_s,
                                                     uint32_t& lo, uint32_t& hi) {
   uint32_t m = kAmaxSeed;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) m = abs_max_bf16x2(m, w[i]);
+  m = abs_max_bf16x2(m, w0);
+  m = abs_max_bf16x2(m, w1);
+  m = abs_max_bf16x2(m, w2);
+  m = abs_max_bf16x2(m, w3);
+  m = abs_max_bf16x2(m, w4);
+  m = abs_max_bf16x2(m, w5);
+  m = abs_max_bf16x2(m, w6);
+  m = abs_max_bf16x2(m, w7);
   float os;
   const uint8_t sfb = block_scale(block_amax(m), s, rcp_s, os);
-  lo = encode8(w[0], w[1], w[2], w[3], os);
-  hi = encode8(w[4], w[5], w[6], w[7], os);
+  lo = encode8(w0, w1, w2, w3, os);
+  hi = encode8(w4, w5, w6, w7, os);
+  return sfb;
+}
+
+// The block's encode multiplier os depends only on its scale byte (for a fixed s), so a caller
+// that quantizes many blocks can tabulate it once: tab[b] = rcp_rn(f32(b) * rcp_rn(s)), the same
+// expression block_scale evaluates.
+__device__ __forceinline__ float os_of_scale_byte(uint32_t b, float rcp_s) {
+  return __frcp_rn(__fmul_rn(ptx::e4m3_to_f32(uint8_t(b)), rcp_s));
+}
+
+// quantize_block16 with the multiplier read from such a table.
+__device__ __forceinline__ uint8_t quantize_block16_tab(uint32_t w0, uint32_t w1, uint32_t w2,
+                                                        uint32_t w3, uint32_t w4, uint32_t w5,
+                                                        uint32_t w6, uint32_t w7, float s,
+                                                        const float* tab, uint32_t& lo,
+                                                        uint32_t& hi) {
+  uint32_t m = kAmaxSeed;
+  m = abs_max_bf16x2(m, w0);
+  m = abs_max_bf16x2(m, w1);
+  m = abs_max_bf16x2(m, w2);
+  m = abs_max_bf16x2(m, w3);
+  m = abs_max_bf16x2(m, w4);
+  m = abs_max_bf16x2(m, w5);
+  m = abs_max_bf16x2(m, w6);
+  m = abs_max_bf16x2(m, w7);
+  const float t = __fmul_rn(__fmul_rn(block_amax(m), s), kRcpE2m1Max);
+  const uint8_t sfb = static_cast<uint8_t>(ptx::f32x2_to_e4m3x2(t, 0.0f) & 0xFFu);
+  const float os = tab[sfb];
+  lo = encode8(w0, w1, w2, w3, os);
+  hi = encode8(w4, w5, w6, w7, os);
   return sfb;
 }
 

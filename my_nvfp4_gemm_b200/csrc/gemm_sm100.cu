@@ -107,7 +107,8 @@ struct Cfg {
   static constexpr int OFF_BAR = OFF_EPI + kNumEpiWarps * EPI_BUFS * EPI_BUF_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 2 * SF_SLOTS + 2 * ACC_STAGES + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
-  static constexpr int SMEM_BYTES = OFF_MISC + 16;
+  static constexpr int OFF_QTAB = OFF_MISC + 16;           // 256 fp32: quantized-output table
+  static constexpr int SMEM_BYTES = OFF_QTAB + 256 * 4;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;     // slack to align the base to 1 KiB
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget exceeded");
 
@@ -461,6 +462,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     const uint32_t buf_s = ptx::smem_u32(buf);
     // TMA swizzle of staging row `lane`: the 16-byte chunk index XOR address bits 7.. of the row
     const uint32_t swz = C::EPI_COLS == 64 ? uint32_t(lane & 7) : uint32_t((lane >> 1) & 3);
+    if constexpr (QOUT) {
+      // Encode multiplier per scale byte, computed once (the per-block reciprocal would cost a
+      // slow-path call with the whole drained row live in registers).
+      const float rcp_s_out = __frcp_rn(__ldg(p.out_scale_ptr));
+      float* tab = reinterpret_cast<float*>(smem + C::OFF_QTAB);
+      for (int i = ew * 32 + lane; i < 256; i += kNumEpiWarps * 32)
+        tab[i] = bq::os_of_scale_byte(uint32_t(i), rcp_s_out);
+      asm volatile("bar.sync 1, %0;" ::"n"(kNumEpiWarps * 32) : "memory");  // epilogue warps only
+    }
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
@@ -501,7 +511,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         // Codes: 128 bytes of this row per tile, staged EPI_ROW_BYTES at a time (each 16-byte
         // chunk = two 16-column blocks); the row's 16 scale bytes go straight to sf_out.
         const float s_out = __ldg(p.out_scale_ptr);
-        const float rcp_s_out = __frcp_rn(s_out);
+        const float* qtab = reinterpret_cast<const float*>(smem + C::OFF_QTAB);
         constexpr int kColsPerChunk = C::EPI_ROW_BYTES * 2;
         uint32_t sfw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
@@ -514,8 +524,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
           for (int k = 0; k < C::EPI_ROW_BYTES / 16; ++k) {
             const int blk = c * (kColsPerChunk / 16) + 2 * k;  // first of the two blocks
             uint32_t lo0, hi0, lo1, hi1;
-            const uint8_t s0 = bq::quantize_block16(&pk[blk * 8], s_out, rcp_s_out, lo0, hi0);
-            const uint8_t s1 = bq::quantize_block16(&pk[blk * 8 + 8], s_out, rcp_s_out, lo1, hi1);
+            const int j = blk * 8;
+            const uint8_t s0 = bq::quantize_block16_tab(pk[j], pk[j + 1], pk[j + 2], pk[j + 3],
+                                                        pk[j + 4], pk[j + 5], pk[j + 6],
+                                                        pk[j + 7], s_out, qtab, lo0, hi0);
+            const uint8_t s1 = bq::quantize_block16_tab(pk[j + 8], pk[j + 9], pk[j + 10],
+                                                        pk[j + 11], pk[j + 12], pk[j + 13],
+                                                        pk[j + 14], pk[j + 15], s_out, qtab, lo1,
+                                                        hi1);
             sfw[blk / 4] |= (uint32_t(s0) | (uint32_t(s1) << 8)) << (8 * (blk % 4));
             ptx::st_shared_v4(row + ((uint32_t(k) ^ swz) << 4), make_uint4(lo0, hi0, lo1, hi1));
           }
