@@ -144,6 +144,20 @@ int nvfp4_gemm_quantized(const void* A, const void* B, const void* A_sf, const v
                          int64_t M, int64_t N, int64_t K, cudaStream_t stream);
 
 /*
+ * Gate+up GEMM with SwiGLU in the epilogue (an MLP's first layer). No reference counterpart:
+ * it replaces gemm_nvfp4 of A against the concatenated [gate; up] weight followed by
+ * silu(gate) * up. B_gate_up holds the 2*I weight rows interleaved in groups of 128 — gate rows
+ * 128t..128t+127, then up rows 128t..128t+127, for t = 0..I/128-1 — with B_gate_up_sf in the
+ * same row order (my_nvfp4_gemm_b200.swiglu.interleave_gate_up builds both). N = 2*I.
+ * out [M, I] bf16 = bf16(silu(Dg) * Du) evaluated in fp32, where Dg, Du are the bf16 values
+ * bf16(A.B^T / scale) of the gate and up columns and silu(x) = x / (1 + exp(-x)).
+ * Requires K % 256 == 0, K > 0, N % 256 == 0; out 16-byte aligned.
+ */
+int nvfp4_gemm_swiglu(const void* A, const void* B_gate_up, const void* A_sf,
+                      const void* B_gate_up_sf, const float* scale, void* out, int64_t M,
+                      int64_t N, int64_t K, cudaStream_t stream);
+
+/*
  * Column-parallel GEMM with the all-gather of D fused into the epilogue (one process per GPU).
  * The reference has no multi-GPU path; this replaces "gemm_nvfp4 on a column shard of B, then an
  * all-gather of the shards' outputs". Every rank passes the same A, its own shard B_shard

@@ -42,6 +42,7 @@ SIGNATURES = {
     "nvfp4_gemm": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P], _INT),
     "nvfp4_gemm_host_scale": ([_P, _P, _P, _P, _F32, _P, _I64, _I64, _I64, _P], _INT),
     "nvfp4_gemm_quantized": ([_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P], _INT),
+    "nvfp4_gemm_swiglu": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P], _INT),
     "nvfp4_gemm_allgather": ([_P, _P, _P, _P, _P, ctypes.POINTER(_P), _INT, _INT, _I64, _I64, _I64, _P], _INT),
     "nvfp4_ipc_export": ([_P, _P, ctypes.POINTER(_I64)], _INT),
     "nvfp4_ipc_open": ([_P, _I64, ctypes.POINTER(_P)], _INT),
@@ -134,6 +135,11 @@ def gemm_quantized(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, out_scale_ptr, q_p
                    k, stream=0) -> int:
     return lib().nvfp4_gemm_quantized(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, out_scale_ptr,
                                       q_ptr, sf_ptr, m, n, k, stream)
+
+
+def gemm_swiglu(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, out_ptr, m, n, k, stream=0) -> int:
+    return lib().nvfp4_gemm_swiglu(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, out_ptr, m, n, k,
+                                   stream)
 
 
 def gemm_allgather(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, output_ptrs, rank, m, n_local, k,

@@ -133,7 +133,7 @@ struct Params {
   int n_blocks;            // tiles along N (BN columns each)
   int k_stages;
   uint64_t timeout_ns;
-  // quantized output (QOUT): D is quantized to NVFP4 with the per-tensor scale *out_scale_ptr;
+  // quantized output (kEpiQuant): D is quantized to NVFP4 with the per-tensor scale *out_scale_ptr;
   // the codes go through the destination map, the scale bytes to sf_out [m][sf_pitch].
   const float* out_scale_ptr;
   uint8_t* sf_out;
@@ -212,9 +212,30 @@ struct DstMaps {
   int count;  // maps in use, 1..NDST
 };
 
-// QOUT: the epilogue quantizes each finished bf16 row to NVFP4 (block_quant.cuh, the same
-// arithmetic as quantize_kernel) and stores codes and scale bytes instead of bf16 D.
-template <class C, int NDST, bool QOUT = false>
+// What the epilogue stores (MODE):
+//   kEpiBf16   : bf16 D;
+//   kEpiQuant  : each finished bf16 row quantized to NVFP4 (block_quant.cuh, the arithmetic of
+//                quantize_kernel): packed codes through the destination map, scale bytes to
+//                p.sf_out;
+//   kEpiSwiglu : the tile's first BN/2 columns are gate and the last BN/2 the matching up
+//                columns (B's rows interleaved that way); stores bf16(silu(g) * u) computed in
+//                fp32 from the bf16 values of g and u, BN/2 output columns per tile.
+constexpr int kEpiBf16 = 0;
+constexpr int kEpiQuant = 1;
+constexpr int kEpiSwiglu = 2;
+
+// silu(x) = x / (1 + exp(-x)) in fp32 (IEEE division, no contraction), as torch evaluates it.
+__device__ __forceinline__ float silu_f32(float x) {
+  return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+}
+
+// bf16 pair of gate values and the matching pair of up values -> bf16 pair of silu(g) * u.
+__device__ __forceinline__ uint32_t swiglu_bf16x2(uint32_t g, uint32_t u) {
+  return ptx::f32x2_to_bf16x2(__fmul_rn(silu_f32(bq::bf16lo_to_f32(g)), bq::bf16lo_to_f32(u)),
+                              __fmul_rn(silu_f32(bq::bf16hi_to_f32(g)), bq::bf16hi_to_f32(u)));
+}
+
+template <class C, int NDST, int MODE = kEpiBf16>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
             const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
@@ -462,7 +483,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     const uint32_t buf_s = ptx::smem_u32(buf);
     // TMA swizzle of staging row `lane`: the 16-byte chunk index XOR address bits 7.. of the row
     const uint32_t swz = C::EPI_COLS == 64 ? uint32_t(lane & 7) : uint32_t((lane >> 1) & 3);
-    if constexpr (QOUT) {
+    if constexpr (MODE == kEpiQuant) {
       // Encode multiplier per scale byte, computed once (the per-block reciprocal would cost a
       // slow-path call with the whole drained row live in registers).
       const float rcp_s_out = __frcp_rn(__ldg(p.out_scale_ptr));
@@ -507,7 +528,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         else ptx::mbar_arrive(&tempty_bar[acc]);
       }
       if (lane == 0) ptx::bulk_wait_group_read<0>();  // the previous tile's stores have read
-      if constexpr (QOUT) {
+      if constexpr (MODE == kEpiQuant) {
         // Codes: 128 bytes of this row per tile, staged EPI_ROW_BYTES at a time (each 16-byte
         // chunk = two 16-column blocks); the row's 16 scale bytes go straight to sf_out.
         const float s_out = __ldg(p.out_scale_ptr);
@@ -553,12 +574,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
           }
         }
       } else {
+      int out_c0 = n0, out_w = p.n;  // output columns of this tile, output width
+      constexpr int kOutCols = MODE == kEpiSwiglu ? C::BN / 2 : C::BN;
+      if constexpr (MODE == kEpiSwiglu) {
 #pragma unroll
-      for (int c = 0; c < C::BN / C::EPI_COLS; ++c) {
+        for (int j = 0; j < C::BN / 4; ++j) pk[j] = swiglu_bf16x2(pk[j], pk[j + C::BN / 4]);
+        out_c0 = n0 / 2;
+        out_w = p.n / 2;
+      }
+#pragma unroll
+      for (int c = 0; c < kOutCols / C::EPI_COLS; ++c) {
         // Boxes entirely outside D (ragged M or N) end the loop — the issued store groups stay a
         // prefix, which the buffer-reuse wait below counts on; boxes that start inside D are
         // clipped by the TMA unit.
-        if (m_cta + ew * 32 >= p.m || n0 + c * C::EPI_COLS >= p.n) break;
+        if (m_cta + ew * 32 >= p.m || out_c0 + c * C::EPI_COLS >= out_w) break;
         const int b = c % C::EPI_BUFS;
         if (c >= C::EPI_BUFS && lane == 0)
           ptx::bulk_wait_group_read<C::EPI_BUFS - 1>();  // buffer b's previous store has read it
@@ -578,7 +607,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
           // Peers' outputs are written over NVLink straight from this staging buffer; the tile
           // reaches every rank while the next tile's MMAs run.
           for (int i = 0; i < (NDST == 1 ? 1 : dst.count); ++i)
-            ptx::tma_store_2d(&dst.map[i], buf + b * C::EPI_BUF_BYTES, n0 + c * C::EPI_COLS,
+            ptx::tma_store_2d(&dst.map[i], buf + b * C::EPI_BUF_BYTES, out_c0 + c * C::EPI_COLS,
                               m_cta + ew * 32);
           ptx::bulk_commit_group();
         }
@@ -670,14 +699,14 @@ constexpr int kMaxDevices = 64;
 
 // Per device, once: raise the dynamic shared-memory limit and find how many CTAs (single) or
 // CTA pairs (clusters of 2) can be resident at once — the persistent grid size.
-template <class C, int NDST, bool QOUT>
+template <class C, int NDST, int MODE>
 int resident_units(int dev) {
   static std::once_flag flags[kMaxDevices];
   static int units[kMaxDevices];
   static cudaError_t errs[kMaxDevices];
   if (dev < 0 || dev >= kMaxDevices) return -NVFP4_ERR_NO_DEVICE;
   std::call_once(flags[dev], [&] {
-    errs[dev] = cudaFuncSetAttribute(gemm_kernel<C, NDST, QOUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    errs[dev] = cudaFuncSetAttribute(gemm_kernel<C, NDST, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      C::SMEM_ALLOC);
     if (errs[dev] != cudaSuccess) return;
     int sms = 0;
@@ -696,7 +725,7 @@ int resident_units(int dev) {
       cfg.attrs = attr;
       cfg.numAttrs = 1;
       int clusters = 0;
-      errs[dev] = cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<C, NDST, QOUT>, &cfg);
+      errs[dev] = cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<C, NDST, MODE>, &cfg);
       units[dev] = clusters > 0 ? clusters : sms / 2;
     } else {
       units[dev] = sms;
@@ -721,20 +750,20 @@ struct DstDesc {
   int count;
 };
 
-// Quantized output of a launch (QOUT): per-tensor scale, scale-byte destination and pitch.
+// Quantized output of a launch (kEpiQuant): per-tensor scale, scale-byte destination, pitch.
 struct QOutDesc {
   const float* out_scale = nullptr;
   uint8_t* sf = nullptr;
   int64_t sf_pitch = 0;
 };
 
-template <class C, int NDST, bool QOUT = false>
+template <class C, int NDST, int MODE = kEpiBf16>
 int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
            const float* scale_ptr, float scale_val, const DstDesc& dd, int64_t M, int64_t N,
            int64_t K, cudaStream_t stream, const QOutDesc& qd = QOutDesc()) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NVFP4_ERR_NO_DEVICE;
-  const int units = resident_units<C, NDST, QOUT>(dev);
+  const int units = resident_units<C, NDST, MODE>(dev);
   if (units <= 0) return units == 0 ? NVFP4_ERR_NO_DEVICE : -units;
   if (dd.count < 1 || dd.count > NDST) return NVFP4_ERR_INVALID_VALUE;
 
@@ -757,9 +786,12 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
   const CUtensorMapSwizzle epi_swizzle =
       C::EPI_ROW_BYTES == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   for (int i = 0; ok && i < dd.count; ++i) {
-    if constexpr (QOUT)  // packed codes [M, N/2]
+    if constexpr (MODE == kEpiQuant)  // packed codes [M, N/2]
       ok = make_map_2d(&dst.map[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, dd.base[i], uint64_t(N) / 2, M,
                        dd.row_bytes, C::EPI_ROW_BYTES, 32, epi_swizzle);
+    else if constexpr (MODE == kEpiSwiglu)  // bf16 [M, N/2]
+      ok = make_map_2d(&dst.map[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dd.base[i], uint64_t(N) / 2,
+                       M, dd.row_bytes, C::EPI_COLS, 32, epi_swizzle);
     else
       ok = make_map_2d(&dst.map[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dd.base[i], N, M,
                        dd.row_bytes, C::EPI_COLS, 32, epi_swizzle);
@@ -794,10 +826,10 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return status_from_cuda(cudaLaunchKernelEx(&cfg, gemm_kernel<C, NDST, QOUT>, tm_a, tm_b, tm_sfa,
+    return status_from_cuda(cudaLaunchKernelEx(&cfg, gemm_kernel<C, NDST, MODE>, tm_a, tm_b, tm_sfa,
                                                tm_sfb, dst, p));
   } else {
-    gemm_kernel<C, NDST, QOUT><<<grid_units, kThreads, C::SMEM_ALLOC, stream>>>(tm_a, tm_b, tm_sfa,
+    gemm_kernel<C, NDST, MODE><<<grid_units, kThreads, C::SMEM_ALLOC, stream>>>(tm_a, tm_b, tm_sfa,
                                                                          tm_sfb, dst, p);
     return status_from_cuda(cudaGetLastError());
   }
@@ -895,8 +927,35 @@ int run_quantized(const void* A, const void* B, const void* A_sf, const void* B_
   qd.sf = static_cast<uint8_t*>(sf_out);
   qd.sf_pitch = N / 16;
   if (M > kRowsPerCta)
-    return launch<CfgPair, 1, true>(A, B, A_sf, B_sf, scale_ptr, 0.0f, dd, M, N, K, stream, qd);
-  return launch<CfgSingle, 1, true>(A, B, A_sf, B_sf, scale_ptr, 0.0f, dd, M, N, K, stream, qd);
+    return launch<CfgPair, 1, kEpiQuant>(A, B, A_sf, B_sf, scale_ptr, 0.0f, dd, M, N, K, stream, qd);
+  return launch<CfgSingle, 1, kEpiQuant>(A, B, A_sf, B_sf, scale_ptr, 0.0f, dd, M, N, K, stream,
+                                         qd);
+}
+
+// Gate+up GEMM with SwiGLU in the epilogue: B holds 2*I rows interleaved in groups of 128 (for
+// each t: gate rows 128t..128t+127, then up rows 128t..128t+127), so every 256-row tile of B
+// carries the gate and up columns of the same 128 features; out [M, I] bf16 =
+// bf16(silu(D_gate) * D_up) with D = bf16(A.B^T / scale) computed in fp32.
+int run_swiglu(const void* A, const void* B, const void* A_sf, const void* B_sf,
+               const float* scale_ptr, float scale_val, void* out, int64_t M, int64_t N,
+               int64_t K, cudaStream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return NVFP4_ERR_INVALID_VALUE;
+  if (K % kBK != 0 || N % 256 != 0 || K == 0) return NVFP4_ERR_UNSUPPORTED_SHAPE;
+  if (M > 0x7FFFFFFF || N > 0x7FFFFFFF || K > 0x7FFFFFFF) return NVFP4_ERR_TOO_LARGE;
+  if (M == 0 || N == 0) return NVFP4_OK;
+  if (!A || !B || !A_sf || !B_sf || !out) return NVFP4_ERR_INVALID_VALUE;
+  if (!aligned_to(A, 16) || !aligned_to(B, 16) || !aligned_to(A_sf, 16) || !aligned_to(B_sf, 16) ||
+      !aligned_to(out, 16))
+    return NVFP4_ERR_MISALIGNED;
+  DstDesc dd = {};
+  dd.base[0] = out;
+  dd.row_bytes = uint64_t(N / 2) * 2;
+  dd.count = 1;
+  if (M > kRowsPerCta)
+    return launch<CfgPair, 1, kEpiSwiglu>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K,
+                                          stream);
+  return launch<CfgSingle, 1, kEpiSwiglu>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K,
+                                          stream);
 }
 
 }  // namespace gemm
@@ -935,6 +994,14 @@ int nvfp4_gemm_quantized(const void* A, const void* B, const void* A_sf, const v
                          int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
   return nvfp4::gemm::run_quantized(A, B, A_sf, B_sf, scale, out_scale, q_out, sf_out, M, N, K,
                                     stream);
+}
+
+int nvfp4_gemm_swiglu(const void* A, const void* B_gate_up, const void* A_sf,
+                      const void* B_gate_up_sf, const float* scale, void* out, int64_t M,
+                      int64_t N, int64_t K, cudaStream_t stream) {
+  if (!scale) return NVFP4_ERR_INVALID_VALUE;
+  return nvfp4::gemm::run_swiglu(A, B_gate_up, A_sf, B_gate_up_sf, scale, 0.0f, out, M, N, K,
+                                 stream);
 }
 
 int nvfp4_gemm_allgather(const void* A, const void* B_shard, const void* A_sf,

@@ -216,6 +216,40 @@ std::tuple<torch::Tensor, torch::Tensor> py_gemm_nvfp4_quantized(
   return std::make_tuple(q, sf);
 }
 
+// Extension (no reference counterpart): gate+up GEMM with SwiGLU in the epilogue. B_gate_up is
+// [2I, K/2] with rows interleaved in groups of 128 (gate, up, gate, up, ...; see
+// my_nvfp4_gemm_b200.swiglu). Returns bf16 [M, I] = bf16(silu(Dg) * Du) in fp32.
+torch::Tensor py_gemm_nvfp4_swiglu(const torch::Tensor& A, const torch::Tensor& B_gate_up,
+                                   const torch::Tensor& A_sf, const torch::Tensor& B_gate_up_sf,
+                                   const torch::Tensor& scale) {
+  TORCH_CHECK(A.dtype() == torch::kUInt8 && A.is_contiguous() && A.dim() == 2 &&
+                  B_gate_up.dtype() == torch::kUInt8 && B_gate_up.is_contiguous() &&
+                  B_gate_up.dim() == 2,
+              "A and B_gate_up must be 2D uint8 and contiguous");
+  TORCH_CHECK(A_sf.dtype() == torch::kFloat8_e4m3fn && A_sf.is_contiguous() &&
+                  B_gate_up_sf.dtype() == torch::kFloat8_e4m3fn && B_gate_up_sf.is_contiguous(),
+              "A_sf and B_gate_up_sf must be float8_e4m3 and contiguous");
+  TORCH_CHECK(scale.dtype() == torch::kFloat32 && 0 == scale.dim() && scale.is_cuda(),
+              "scale must be a float32 scalar on the GPU");
+  TORCH_CHECK(A.is_cuda() && B_gate_up.device() == A.device() && A_sf.device() == A.device() &&
+                  B_gate_up_sf.device() == A.device() && scale.device() == A.device(),
+              "all tensors must be on the same cuda device");
+  const int64_t M = A.size(0), N = B_gate_up.size(0), K = A.size(1) * 2;
+  TORCH_CHECK(B_gate_up.size(1) * 2 == K, "A and B_gate_up must have the same K");
+  TORCH_CHECK(K % 256 == 0 && K > 0, "K must be a positive multiple of 256, got ", K);
+  TORCH_CHECK(N % 256 == 0, "B_gate_up must have a multiple of 256 rows (2*I, I % 128 == 0), got ", N);
+  TORCH_CHECK(A_sf.numel() == M * (K / 16) && B_gate_up_sf.numel() == N * (K / 16),
+              "scale-factor tensors must hold [rows, K/16] factors");
+  const c10::cuda::CUDAGuard guard(A.device());
+  auto out = torch::empty({M, N / 2}, torch::dtype(torch::kBFloat16).device(A.device()));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(A.device().index());
+  check_status(nvfp4_gemm_swiglu(A.data_ptr(), B_gate_up.data_ptr(), A_sf.data_ptr(),
+                                 B_gate_up_sf.data_ptr(), scale.data_ptr<float>(), out.data_ptr(),
+                                 M, N, K, stream),
+               "gemm_nvfp4_swiglu");
+  return out;
+}
+
 // Extension (no reference counterpart): the column-parallel GEMM with the all-gather fused into
 // its epilogue. `output` is this rank's full D [M, world * N_local] (bf16, contiguous) and
 // `output_ptrs[r]` the address, in this process, of rank r's D (output_ptrs[rank] ==
@@ -331,6 +365,10 @@ PYBIND11_MODULE(my_plugins, m) {
         "GEMM with the output quantized to NVFP4 in the epilogue; returns (packed, sf)",
         py::arg("A"), py::arg("B"), py::arg("A_sf"), py::arg("B_sf"), py::arg("scale"),
         py::arg("out_scale"));
+  m.def("gemm_nvfp4_swiglu", &py_gemm_nvfp4_swiglu,
+        "gate+up GEMM with SwiGLU in the epilogue; B_gate_up rows interleaved in groups of 128",
+        py::arg("A"), py::arg("B_gate_up"), py::arg("A_sf"), py::arg("B_gate_up_sf"),
+        py::arg("scale"));
   m.def("gemm_nvfp4_allgather", &py_gemm_nvfp4_allgather,
         "column-parallel GEMM storing this rank's columns into every rank's output",
         py::arg("A"), py::arg("B_shard"), py::arg("A_sf"), py::arg("B_sf_shard"), py::arg("scale"),
