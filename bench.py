@@ -55,6 +55,9 @@ def parse_args():
     ap.add_argument("--m", type=int, default=128, help="decode tokens (16, 32, 64, 128)")
     ap.add_argument("--gather", action="store_true",
                     help="prefill/decode: include the chunked NCCL all-gather of D in the timing")
+    ap.add_argument("--swiglu", action="store_true",
+                    help="prefill: the weight is gate+up (2 x 28672 rows); SwiGLU in the GEMM "
+                         "epilogue, output [M, 28672]")
     ap.add_argument("--fused-gather", action="store_true",
                     help="with --gather: the all-gather fused into the GEMM epilogue (stores into "
                          "every rank's output over NVLink) instead of NCCL")
@@ -498,7 +501,11 @@ def run_sharded_workload(args):
         M, N, seed, frac, name = args.m, 28672, 3, 0.0, f"decode_m{args.m}_n28672_k8192"
     else:
         M, N, seed, frac, name = 16384, 57344, 4, 0.005, "prefill_16384x57344x8192"
-    n0, n1 = sharded.shard_range(N, world, rank)
+    swiglu = bool(args.swiglu and args.workload == "prefill")
+    if swiglu and args.gather:
+        raise SystemExit("--swiglu and --gather are separate measurements")
+    # SwiGLU keeps each rank's gate/up row pairs together: shards of whole 256-row groups
+    n0, n1 = sharded.shard_range(N, world, rank, align=256 if swiglu else 128)
     g = torch.Generator(device="cuda").manual_seed(seed)
     X = torch.randn(M, K, device="cuda", generator=g)
     if frac:
@@ -512,7 +519,16 @@ def run_sharded_workload(args):
     gw = torch.Generator(device="cuda").manual_seed(seed + 1000)
     W = (torch.randn(N, K, device="cuda", generator=gw) * 0.02).to(torch.bfloat16)
     sW = (6 * 448 / W.abs().max().to(torch.float32)).reshape(())
-    w, w_sf = plugins.quantize_nvfp4(W[n0:n1].contiguous(), sW)
+    if swiglu:
+        from my_nvfp4_gemm_b200.swiglu import interleave_gate_up
+        half = N // 2
+        wq, wq_sf = plugins.quantize_nvfp4(W, sW)          # rows [gate; up]
+        wi = interleave_gate_up(wq[:half], wq[half:])
+        wi_sf = interleave_gate_up(wq_sf[:half].view(torch.uint8), wq_sf[half:].view(torch.uint8))
+        w, w_sf = wi[n0:n1].contiguous(), wi_sf[n0:n1].contiguous().view(torch.float8_e4m3fn)
+        del wq, wq_sf, wi, wi_sf
+    else:
+        w, w_sf = plugins.quantize_nvfp4(W[n0:n1].contiguous(), sW)
     del W
     torch.cuda.empty_cache()
     scale = (sX * sW).reshape(())
@@ -523,7 +539,15 @@ def run_sharded_workload(args):
     ptrs = (x.data_ptr(), w.data_ptr(), x_sf.data_ptr(), w_sf.data_ptr(), scale.data_ptr(), d.data_ptr())
 
     fused = bool(args.gather and args.fused_gather and world > 1)
-    if args.gather and world > 1:
+    if swiglu:
+        out = torch.empty(M, n_loc // 2, dtype=torch.bfloat16, device="cuda")
+
+        def step():
+            st = capi.gemm_swiglu(x.data_ptr(), w.data_ptr(), x_sf.data_ptr(), w_sf.data_ptr(),
+                                  scale.data_ptr(), out.data_ptr(), M, n_loc, K, stream_h)
+            if st:
+                raise capi.NvFp4Error(st, "nvfp4_gemm_swiglu")
+    elif args.gather and world > 1:
         def step():
             sharded.gemm_column_parallel(x, w, x_sf, w_sf, scale, gather=True, chunks=4,
                                          fused=fused)
@@ -551,6 +575,8 @@ def run_sharded_workload(args):
         "config": {"workload": name, "M": M, "N": N, "K": K, "n_per_rank": n_loc,
                    "parallelism": f"column-parallel N x{world}",
                    "all_gather_in_timing": bool(args.gather and world > 1),
+                   "epilogue": ("SwiGLU (gate+up interleaved in 128-row groups), output "
+                                f"[M, {N // 2}]" if swiglu else "bf16 D"),
                    "all_gather": ("fused into the GEMM epilogue (NVLink stores)" if fused else
                                   "NCCL all_gather_into_tensor, 4 chunks" if args.gather and world > 1
                                   else None),
@@ -563,6 +589,22 @@ def run_sharded_workload(args):
         "gpu_launches": args.steps * (1 if fused else 4 if (args.gather and world > 1) else 1),
         "clocks": sampler.summary(),
     }
+    if swiglu and world == 1:
+        # the unfused equivalent: bf16 D of the gate+up GEMM, then torch silu(g) * u
+        import torch.nn.functional as F
+        d_full = torch.empty(M, n_loc, dtype=torch.bfloat16, device="cuda")
+        half = n_loc // 2
+
+        def unfused():
+            capi.check(capi.gemm(x.data_ptr(), w.data_ptr(), x_sf.data_ptr(), w_sf.data_ptr(),
+                                 scale.data_ptr(), d_full.data_ptr(), M, n_loc, K, stream_h),
+                       "nvfp4_gemm")
+            (F.silu(d_full[:, :half].float()) * d_full[:, half:].float()).to(torch.bfloat16)
+
+        n_u = max(3, min(args.steps, 10))
+        t_u = time_device(torch, unfused, n_u, args.warmup, flush, world) / n_u
+        line["gemm_then_torch_silu_mul_ms"] = t_u
+        del d_full
     if args.gather and world > 1:
         # roofline of the GEMM with its gather: the slower of the tensor bound and this rank's
         # output bytes over NVLink (measured 770 GB/s per direction per GPU on this pool)
