@@ -304,6 +304,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   ptx::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Programmatic dependent launch (single-destination launches): the grid is launched as soon as
+  // every CTA of the previous kernel on the stream has exited, and the setup above (barriers,
+  // TMEM, descriptor prefetch) overlaps that kernel's completion. It touches no global memory;
+  // every thread waits for the previous kernel's completion before its first global access.
+  // There is no early trigger for the next kernel: CTAs that launch into the SMs this grid leaves
+  // idle, and wait there, slowed the decode-shape main loop by ~12 % in measurements.
+  if constexpr (NDST == 1) ptx::griddep_wait();
+
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -616,10 +624,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       if (++acc == C::ACC_STAGES) { acc = 0; acc_phase ^= 1; }
     }
     if (lane == 0) {
-      ptx::bulk_wait_group<0>();
-      // Stores into other GPUs' memory must be visible system-wide before the kernel ends
-      // (the caller orders the ranks' reads after every rank's kernel).
-      if constexpr (NDST > 1) __threadfence_system();
+      if constexpr (NDST > 1) {
+        // Stores into other GPUs' memory must be complete and visible system-wide before the
+        // kernel ends (the caller orders the ranks' reads after every rank's kernel).
+        ptx::bulk_wait_group<0>();
+        __threadfence_system();
+      } else {
+        // Local stores only need their shared-memory reads done before the CTA exits; the
+        // grid's completion covers the global writes.
+        ptx::bulk_wait_group_read<0>();
+      }
     }
   }
 
@@ -813,26 +827,31 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
   const int64_t tiles = int64_t(p.m_blocks) * p.n_blocks;
   if (tiles > 0x7FFFFFFF / 2) return NVFP4_ERR_TOO_LARGE;
   const int grid_units = int(tiles < units ? tiles : units);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  int na = 0;
   if constexpr (C::PAIR) {
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(2 * grid_units);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = C::SMEM_ALLOC;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return status_from_cuda(cudaLaunchKernelEx(&cfg, gemm_kernel<C, NDST, MODE>, tm_a, tm_b, tm_sfa,
-                                               tm_sfb, dst, p));
-  } else {
-    gemm_kernel<C, NDST, MODE><<<grid_units, kThreads, C::SMEM_ALLOC, stream>>>(tm_a, tm_b, tm_sfa,
-                                                                         tm_sfb, dst, p);
-    return status_from_cuda(cudaGetLastError());
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 2;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   }
+  if constexpr (NDST == 1) {
+    // The grid may launch once the previous kernel's CTAs have exited and set up while that
+    // kernel completes; the kernel waits for the completion before touching global memory.
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.gridDim = dim3(C::CTAS * grid_units);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::SMEM_ALLOC;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return status_from_cuda(cudaLaunchKernelEx(&cfg, gemm_kernel<C, NDST, MODE>, tm_a, tm_b, tm_sfa,
+                                             tm_sfb, dst, p));
 }
 
 int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const float* scale_ptr,

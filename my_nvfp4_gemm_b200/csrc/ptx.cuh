@@ -87,6 +87,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Programmatic dependent launch: block until the grids this one depends on (the previous kernel
+// on the stream, when this grid was launched with programmatic stream serialization) have
+// completed and their memory operations are visible; returns at once otherwise.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Streaming 16-byte global load that does not allocate in L1 (read-once data).
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
   uint4 v;

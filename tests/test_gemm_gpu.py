@@ -251,5 +251,67 @@ def test_gemm_rejects_bad_shapes(plugins):
                            torch.zeros(4, 8, device="cuda").to(e4), torch.zeros(8, 16, device="cuda").to(e4), s)
 
 
+@pytest.mark.parametrize("M,N,K", [(96, 2048, 4096), (512, 1024, 2048)])
+def test_gemm_orders_after_previous_kernels(M, N, K):
+    """The GEMM is launched with programmatic stream serialization (it may set up before the
+    previous kernel on the stream has completed) and waits for that kernel before touching
+    memory: operands written by the kernel just before it are read in full, and an output buffer
+    that the kernel just before it reads is not overwritten early. Consecutive GEMMs (the same
+    with the epilogue of one and the loads of the next) are covered by the back-to-back launches
+    of test_gemm_back_to_back_launches. Six launches alternate between two problems with no
+    synchronisation in between."""
+    rng = np.random.default_rng(11 + M)
+    problems = [random_operands(rng, M, N, K) for _ in range(2)]
+    refs = [capi_gemm(*pr, 1.0) for pr in problems]
+    assert not np.array_equal(refs[0], refs[1])
+    dev = [to_dev(*pr) for pr in problems]
+    bufs = [torch.empty_like(t) for t in dev[0]]
+    d = torch.empty(M, N, dtype=torch.int16, device="cuda")
+    s = torch.tensor(1.0, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    snaps = []
+    for it in range(6):
+        for dst, src in zip(bufs, dev[it % 2]):
+            torch.bitwise_xor(src, 0, out=dst)   # an elementwise kernel writes each operand
+        capi.check(capi.gemm(bufs[0].data_ptr(), bufs[1].data_ptr(), bufs[2].data_ptr(),
+                             bufs[3].data_ptr(), s.data_ptr(), d.data_ptr(), M, N, K, stream),
+                   "nvfp4_gemm")
+        snaps.append(torch.bitwise_xor(d, 0))   # a kernel reads D before the next GEMM writes it
+    torch.cuda.synchronize()
+    for it, snap in enumerate(snaps):
+        assert np.array_equal(snap.cpu().numpy().view(np.uint16), refs[it % 2]), f"launch {it}"
+
+
+@pytest.mark.parametrize("M", [16, 300])
+def test_gemm_back_to_back_launches(M):
+    """GEMM after GEMM with no other kernel in between: the first M*K/2 bytes of each output
+    are read as the next launch's A (packed codes [M, K/2]), a chain of 8 launches on one
+    stream. A launch that read A before the previous one's stores were complete would diverge
+    from the same chain run with a synchronisation after every launch."""
+    rng = np.random.default_rng(40 + M)
+    K, N = 1024, 512                      # D is bf16 [M, 512]: M*K bytes, twice the next A
+    a, b, asf, bsf = to_dev(*random_operands(rng, M, N, K))
+    s = torch.tensor(1.0, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    bufs = [torch.empty(M, N, dtype=torch.bfloat16, device="cuda") for _ in range(8)]
+
+    def chain(sync):
+        src = a.data_ptr()
+        for i in range(8):
+            capi.check(capi.gemm(src, b.data_ptr(), asf.data_ptr(), bsf.data_ptr(),
+                                 s.data_ptr(), bufs[i].data_ptr(), M, N, K, stream),
+                       "nvfp4_gemm")
+            if sync:
+                torch.cuda.synchronize()
+            src = bufs[i].data_ptr()
+        torch.cuda.synchronize()
+        return [t.clone() for t in bufs]
+
+    ref = chain(True)
+    for _ in range(2):
+        assert all(torch.equal(x.view(torch.int16), y.view(torch.int16))
+                   for x, y in zip(chain(False), ref))
+
+
 def test_no_device_timeouts_recorded():
     assert capi.device_status(torch.cuda.current_stream().cuda_stream) == 0
