@@ -640,6 +640,8 @@ def run_sharded_workload(args):
                      "achieved_tflops": achieved_tf, "frac_fp4_peak": achieved_tf / (4 * bf16_tf),
                      "achieved_gbs": achieved_gbs, "frac_hbm": achieved_gbs / hbm_gbs,
                      "algorithmic_bytes_per_rank": bytes_rank,
+                     "traffic": (profiled_traffic(f"gemm_decode_m{M}")
+                                 if args.workload == "decode" and world == 1 else None),
                      "peak_source": f"{peak_src}: HBM {hbm_gbs} GB/s, FP4 4 x bf16 {bf16_tf} TF/s"},
         "gpu_launches": args.steps * (1 if fused else 4 if (args.gather and world > 1) else 1),
         "clocks": sampler.summary(),
