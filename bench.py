@@ -39,6 +39,25 @@ NOMINAL_FP4_TFLOPS = 9000.0
 QUANT_BYTES = 8192 * 8192 * 2 + 8192 * 4096 + 8192 * 512   # 171,966,464 per pass
 
 
+_RESULT_OUT = None
+
+
+def keep_stdout_for_result():
+    """Reserve the process's stdout for the one JSON result line: keep a private duplicate of
+    file descriptor 1 for it and point descriptor 1 at stderr, so banners that libraries print
+    to stdout (NCCL prints its version line at communicator creation when NCCL_DEBUG asks for
+    it) end up on stderr."""
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
+def emit(line):
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    print(json.dumps(line), file=out, flush=True)
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -306,7 +325,7 @@ def run_reference_arm(args):
             "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -527,7 +546,7 @@ def run_ours(args):
     if st != 0:
         line["device_status"] = capi.STATUS_NAMES.get(st, st)
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -688,7 +707,7 @@ def run_sharded_workload(args):
                                       "bound_ms": bound_ms, "frac": bound_ms / ms,
                                       "nvlink_gbs_per_direction": 770.0}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
         sharded.release_peer_outputs()
@@ -699,6 +718,7 @@ def run_sharded_workload(args):
 
 def main():
     args = parse_args()
+    keep_stdout_for_result()
     if args.impl == "reference":
         return run_reference_arm(args)
     if args.workload != "square":
