@@ -487,6 +487,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     const int ew = warp - kFirstEpiWarp;  // == warp % 4: TMEM lanes 32*ew .. 32*ew+31
     const float scale = p.scale_ptr ? __ldg(p.scale_ptr) : p.scale_val;
     const float alpha = __frcp_rn(scale);
+    const uint64_t alpha2 = ptx::f32x2_splat(alpha);
     uint8_t* buf = sEPI + ew * C::EPI_BUFS * C::EPI_BUF_BYTES;
     const uint32_t buf_s = ptx::smem_u32(buf);
     // TMA swizzle of staging row `lane`: the 16-byte chunk index XOR address bits 7.. of the row
@@ -522,11 +523,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         ptx::tmem_ld_32x32b_x32(t_row + g * 64 + 32, r1);
         ptx::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          pk[g * 32 + i] = ptx::f32x2_to_bf16x2(__uint_as_float(r0[2 * i]) * alpha,
-                                                __uint_as_float(r0[2 * i + 1]) * alpha);
-          pk[g * 32 + 16 + i] = ptx::f32x2_to_bf16x2(__uint_as_float(r1[2 * i]) * alpha,
-                                                     __uint_as_float(r1[2 * i + 1]) * alpha);
+        for (int i = 0; i < 16; ++i) {  // acc * (1/scale), two columns per multiply
+          pk[g * 32 + i] = ptx::scaled_f32x2_to_bf16x2(r0[2 * i], r0[2 * i + 1], alpha2);
+          pk[g * 32 + 16 + i] = ptx::scaled_f32x2_to_bf16x2(r1[2 * i], r1[2 * i + 1], alpha2);
         }
       }
       ptx::tc_fence_before_sync();

@@ -74,6 +74,25 @@ __device__ __forceinline__ uint32_t f32x2_to_bf16x2(float lo, float hi) {
   return out;
 }
 
+// {alpha, alpha} as a packed f32x2 operand.
+__device__ __forceinline__ uint64_t f32x2_splat(float alpha) {
+  uint64_t out;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(out) : "r"(__float_as_uint(alpha)));
+  return out;
+}
+
+// bf16x2 of (lo * alpha, hi * alpha) for two fp32 bit patterns: one packed f32x2 multiply
+// (each lane rounded to nearest even, as __fmul_rn) and one conversion.
+__device__ __forceinline__ uint32_t scaled_f32x2_to_bf16x2(uint32_t lo, uint32_t hi,
+                                                           uint64_t alpha2) {
+  uint64_t v, p;
+  uint32_t plo, phi;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(lo), "r"(hi));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(v), "l"(alpha2));
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(plo), "=r"(phi) : "l"(p));
+  return f32x2_to_bf16x2(__uint_as_float(plo), __uint_as_float(phi));
+}
+
 // ----------------------------------------------------------------------------------------
 // Addresses, timers, loads/stores
 // ----------------------------------------------------------------------------------------
