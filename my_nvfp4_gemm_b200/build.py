@@ -67,8 +67,9 @@ def build_lib(force: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=len(jobs) or 1) as ex:
         list(ex.map(_run, jobs))
     out = lib_path()
-    if force or jobs or _newer(out, objs):
-        _run([NVCC, "-shared"] + ARCH + ["-o", out] + objs)
+    exports = os.path.join(CSRC, "exports.map")
+    if force or jobs or _newer(out, objs + [exports]):
+        _run([NVCC, "-shared"] + ARCH + ["-Xlinker", f"--version-script={exports}", "-o", out] + objs)
     return out
 
 

@@ -161,7 +161,7 @@ __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& mb, 
 // warp reads its rows' factors for k-block c of the shared-memory slot (16 bytes per row =
 // K-steps 0..3) and writes its quarter of the stage's TMEM slot with tcgen05.st:
 //   slot + j*(BN/32) + i   <- step-j word of B row 32i + lane     (BN/8 columns)
-//   slot + BN/8 + 4j + k   <- step-j word of A row 32q + lane     (16 columns, k = 0..3)
+//   slot + BN/8 + 4j + q   <- step-j word of A row 32q + lane     (4 of the 16 A columns)
 //
 // Shared-memory address of k-block c's 16 bytes of row `row` in a scale-factor slot. The TMA
 // unit's 32B/64B swizzle XORs the 16-byte chunk index with address bits 7 and up of the row.
@@ -185,20 +185,18 @@ __device__ __forceinline__ void write_sf_slot(uint32_t slot, uint32_t sfa_s, uin
     vb[3 * kChunksB + i] = w.w;
   }
   const uint4 a = ptx::ld_shared_v4(sf_chunk_addr<C>(sfa_s, 32 * q + lane, c));
-  uint32_t va[16];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    va[0 + k] = a.x;
-    va[4 + k] = a.y;
-    va[8 + k] = a.z;
-    va[12 + k] = a.w;
-  }
   if constexpr (C::BN == 256) {
     ptx::tmem_st_32x32b_x32(slot, vb);
   } else {
     ptx::tmem_st_32x32b_x16(slot, vb);
   }
-  ptx::tmem_st_32x32b_x16(slot + C::BN / 8, va);
+  // A: quarter q's MMA reads K-step j's factors from column BN/8 + 4j + q only; the other three
+  // columns of each group belong to the other quarters' lanes and are left alone.
+  const uint32_t sfa = slot + C::BN / 8 + uint32_t(q);
+  ptx::tmem_st_32x32b_x1(sfa + 0, a.x);
+  ptx::tmem_st_32x32b_x1(sfa + 4, a.y);
+  ptx::tmem_st_32x32b_x1(sfa + 8, a.z);
+  ptx::tmem_st_32x32b_x1(sfa + 12, a.w);
 }
 
 // Where the epilogue stores D: NDST = 1 for the plain GEMM; the column-parallel form with a

@@ -29,6 +29,21 @@ def test_every_declared_symbol_is_exported():
     assert set(names) == set(capi.SIGNATURES), "ctypes signatures out of sync with the header"
 
 
+def test_only_the_c_abi_is_exported():
+    """Kernel stubs and C++ helpers are local to the library (linker version script): a second
+    build loaded into the same process cannot resolve to this one's kernels."""
+    import shutil
+    import subprocess
+    if shutil.which("nm") is None:
+        pytest.skip("nm not available")
+    out = subprocess.run(["nm", "-D", "--defined-only", capi._build.lib_path()], check=True,
+                         capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    exported = {n.split("@")[0] for n in exported}
+    assert exported, "no exported symbols"
+    assert exported == set(declared_functions()), sorted(exported ^ set(declared_functions()))
+
+
 def test_status_strings_and_version():
     assert capi.status_string(0) == "NVFP4_OK"
     for code, name in capi.STATUS_NAMES.items():
