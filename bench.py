@@ -673,6 +673,10 @@ def run_sharded_workload(args):
                           "back: every call reads its weight from HBM" if rotate else
                           "flushed (256 MiB write) before every timed step")},
         "roofline": {"bound": "hbm" if M <= 128 else "tensor",
+                     "achieved": achieved_gbs if M <= 128 else achieved_tf,
+                     "peak": hbm_gbs if M <= 128 else 4 * bf16_tf,
+                     "unit": "GB/s" if M <= 128 else "TFLOP/s",
+                     "frac": (achieved_gbs / hbm_gbs) if M <= 128 else achieved_tf / (4 * bf16_tf),
                      "achieved_tflops": achieved_tf, "frac_fp4_peak": achieved_tf / (4 * bf16_tf),
                      "achieved_gbs": achieved_gbs, "frac_hbm": achieved_gbs / hbm_gbs,
                      "algorithmic_bytes_per_rank": bytes_rank,
