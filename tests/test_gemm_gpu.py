@@ -169,6 +169,32 @@ def test_gemm_n_and_m_sharding_bit_identical(plugins):
     assert np.array_equal(top, full[:200])
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 528, 2560), (96, 1024, 512), (1024, 2048, 2048)])
+def test_gemm_allgather_on_one_gpu_matches_gemm(M, N, K):
+    """The GEMM with the all-gather fused into its epilogue, with every rank's output a buffer on
+    this one GPU: rank r stores its column shard into every rank's output, so after the calls of
+    ranks 0 and 1 both outputs equal the plain GEMM bit for bit (world 1: the one output does).
+    Covers the multi-destination epilogue and its configuration without a second GPU."""
+    rng = np.random.default_rng(M + N + K)
+    A, B, Asf, Bsf = random_operands(rng, M, N, K)
+    full = capi_gemm(A, B, Asf, Bsf, 1.25)
+    a, asf = to_dev(A, Asf)
+    s = torch.tensor(1.25, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for world in (1, 2):
+        n_loc = N // world
+        outs = [torch.full((M, N), -1, dtype=torch.int16, device="cuda") for _ in range(world)]
+        for r in range(world):
+            b, bsf = to_dev(B[r * n_loc:(r + 1) * n_loc], Bsf[r * n_loc:(r + 1) * n_loc])
+            capi.check(capi.gemm_allgather(a.data_ptr(), b.data_ptr(), asf.data_ptr(), bsf.data_ptr(),
+                                           s.data_ptr(), [o.data_ptr() for o in outs], r, M, n_loc, K,
+                                           stream), "nvfp4_gemm_allgather")
+            torch.cuda.synchronize()
+        for i, o in enumerate(outs):
+            got = o.cpu().numpy().view(np.uint16)
+            assert np.array_equal(got, full), f"world {world}: output of rank {i} differs"
+
+
 def test_gemm_deterministic(plugins):
     rng = np.random.default_rng(9)
     A, B, Asf, Bsf = random_operands(rng, 1000, 1024, 4096)
