@@ -753,12 +753,6 @@ using CfgSingle = Cfg<256, 4, 1, false, 1, 4>;
 // per shared-memory slot (64-byte rows, 2 slots), one 32 x 64 staging box per epilogue warp;
 // tensor memory 256 + 5 x 48 columns.
 using CfgPair = Cfg<256, 5, 1, true, 4, 2, 64, 1>;
-// The same tiles for the GEMM with the all-gather fused into the epilogue: every staged box also
-// goes to the other ranks over NVLink, and a box's shared memory is free only once those copies
-// have read it, so each epilogue warp gets two staging boxes (one is filled while the other is
-// still being sent); the 16 KiB they need come from scale-factor slots of 32-byte rows (two
-// k-blocks per load, still whole sectors).
-using CfgPairGather = Cfg<256, 5, 1, true, 2, 2, 64, 2>;
 
 // D of this launch: `count` destinations, each [M, N] with its own base and row pitch.
 struct DstDesc {
@@ -919,8 +913,8 @@ int run_allgather(const void* A, const void* B, const void* A_sf, const void* B_
   if (!aligned_to(A, 16) || !aligned_to(B, 16) || !aligned_to(A_sf, 16) || !aligned_to(B_sf, 16))
     return NVFP4_ERR_MISALIGNED;
   if (M > kRowsPerCta)
-    return launch<CfgPairGather, kMaxRanks>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M,
-                                            N_local, K, stream);
+    return launch<CfgPair, kMaxRanks>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N_local, K,
+                                      stream);
   return launch<CfgSingle, kMaxRanks>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N_local, K,
                                       stream);
 }
