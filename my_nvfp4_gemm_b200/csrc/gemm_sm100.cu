@@ -96,8 +96,6 @@ struct Cfg {
   static constexpr int B_STAGE = B_ROWS * kBKBytes;
   static constexpr int SFA_SLOT = kRowsPerCta * SF_ROW_BYTES;
   static constexpr int SFB_SLOT = BN * SF_ROW_BYTES;       // every CTA holds all BN rows
-  static constexpr uint32_t AB_TX = uint32_t(CTAS) * (A_STAGE + B_STAGE);  // pair total
-  static constexpr uint32_t SF_TX = SFA_SLOT + SFB_SLOT;                   // per CTA
 
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
@@ -132,6 +130,11 @@ struct Params {
   int m_blocks;            // tiles along M (TILE_M rows each)
   int n_blocks;            // tiles along N (BN columns each)
   int k_stages;
+  // transaction bytes of one A/B fill (the pair's total) and of one scale-factor slot (this
+  // CTA's): the A and A-scale boxes cover a_rows rows (kRowsPerCta, or M for a single-CTA
+  // launch with M < kRowsPerCta)
+  uint32_t ab_tx;
+  uint32_t sf_tx;
   uint64_t timeout_ns;
   // quantized output (kEpiQuant): D is quantized to NVFP4 with the per-tensor scale *out_scale_ptr;
   // the codes go through the destination map, the scale bytes to sf_out [m][sf_pitch].
@@ -323,7 +326,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         for (int kb = 0; kb < p.k_stages; ++kb) {
           if (!ptx::mbar_wait<kPair>(&empty_bar[stage], phase ^ 1, abort_flag, p.timeout_ns))
             goto producer_done;
-          if (rank == 0) ptx::mbar_arrive_expect_tx(&full_bar[stage], C::AB_TX);
+          if (rank == 0) ptx::mbar_arrive_expect_tx(&full_bar[stage], p.ab_tx);
           if constexpr (kPair) {
             ptx::tma_load_2d_pair(sA + stage * C::A_STAGE, &tm_a, &full_bar[stage], kb * kBKBytes, m_cta);
             ptx::tma_load_2d_pair(sB + stage * C::B_STAGE, &tm_b, &full_bar[stage], kb * kBKBytes, n_cta);
@@ -361,7 +364,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         for (int kb = 0; kb < p.k_stages; kb += C::SF_KB) {
           if (!ptx::mbar_wait<kPair>(&sempty_bar[slot], phase ^ 1, abort_flag, p.timeout_ns))
             goto sf_producer_done;
-          ptx::mbar_arrive_expect_tx(&sfull_bar[slot], C::SF_TX);
+          ptx::mbar_arrive_expect_tx(&sfull_bar[slot], p.sf_tx);
           ptx::tma_load_2d(sSFA + slot * C::SFA_SLOT, &tm_sfa, &sfull_bar[slot],
                            kb * kSfBytesPerRow, row_a);
           ptx::tma_load_2d(sSFB + slot * C::SFB_SLOT, &tm_sfb, &sfull_bar[slot],
@@ -786,12 +789,17 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
   const CUtensorMapSwizzle sf_swizzle = C::SF_ROW_BYTES == 64   ? CU_TENSOR_MAP_SWIZZLE_64B
                                         : C::SF_ROW_BYTES == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                                                 : CU_TENSOR_MAP_SWIZZLE_NONE;
-  bool ok = make_map_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, kb, M, kb, kBKBytes, kRowsPerCta,
+  // A single-CTA launch with M < kRowsPerCta (decode shapes) loads only the M rows of A and of
+  // its scale factors that exist: a 128-row box would have the TMA unit fill the missing rows
+  // with zeros on every fill. The MMA still runs 128 rows; the shared-memory rows past M hold
+  // stale bytes, and their results (TMEM lanes past M) are never stored.
+  const uint32_t a_rows = (!C::PAIR && M < kRowsPerCta) ? uint32_t(M) : uint32_t(kRowsPerCta);
+  bool ok = make_map_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, A, kb, M, kb, kBKBytes, a_rows,
                         CU_TENSOR_MAP_SWIZZLE_128B) &&
             make_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, B, kb, N, kb, kBKBytes, C::B_ROWS,
                         CU_TENSOR_MAP_SWIZZLE_128B) &&
             make_map_2d(&tm_sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, A_sf, ks, M, ks, C::SF_ROW_BYTES,
-                        kRowsPerCta, sf_swizzle) &&
+                        a_rows, sf_swizzle) &&
             make_map_2d(&tm_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, B_sf, ks, N, ks, C::SF_ROW_BYTES,
                         C::BN, sf_swizzle);
   const CUtensorMapSwizzle epi_swizzle =
@@ -817,6 +825,8 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
   p.m_blocks = int((M + C::TILE_M - 1) / C::TILE_M);
   p.n_blocks = int((N + C::BN - 1) / C::BN);
   p.k_stages = int(K / kBK);
+  p.ab_tx = uint32_t(C::CTAS) * (a_rows * kBKBytes + C::B_STAGE);
+  p.sf_tx = a_rows * C::SF_ROW_BYTES + C::SFB_SLOT;
   p.timeout_ns = 2000000000ull;  // 2 s per wait: far above any legitimate stall
   p.out_scale_ptr = qd.out_scale;
   p.sf_out = qd.sf;
