@@ -129,8 +129,9 @@ __device__ __forceinline__ uint8_t ld_nc_u8(const void* p) {
   asm volatile("ld.global.nc.u8 %0, [%1];" : "=h"(v) : "l"(p));
   return static_cast<uint8_t>(v);
 }
-__device__ __forceinline__ void st_v4(void* p, uint4 v) {
-  asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+// Streaming 16-byte global store (.cs: cached evict-first, for large outputs written once).
+__device__ __forceinline__ void st_stream_v4(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w)
                : "memory");
 }

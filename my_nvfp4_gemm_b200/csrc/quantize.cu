@@ -98,7 +98,7 @@ dequantize_kernel(const uint32_t* __restrict__ q, const float* __restrict__ scal
       o[i] = ptx::f32x2_to_bf16x2(__fmul_rn(__low2float(p), scale),
                                   __fmul_rn(__high2float(p), scale));
     }
-    if (h < n_half_blocks) ptx::st_v4(y + h, make_uint4(o[0], o[1], o[2], o[3]));
+    if (h < n_half_blocks) ptx::st_stream_v4(y + h, make_uint4(o[0], o[1], o[2], o[3]));
   }
 }
 
