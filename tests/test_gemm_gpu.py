@@ -86,6 +86,9 @@ SHAPES = [
     (300, 520, 2560),
     (1024, 1024, 2048),
     (16, 4096, 8192),    # decode-like, long K
+    (5, 520, 1024),      # M < 128: only the M existing rows of A are loaded
+    (127, 264, 512),
+    (63, 1024, 2048),
 ]
 
 

@@ -16,7 +16,8 @@ def _operands(M, N, K, seed):
 
 
 @pytest.mark.parametrize("M,N,K", [(512, 768, 1024), (96, 512, 512), (300, 416, 768),
-                                   (128, 28672, 8192), (2048, 4096, 4096)])
+                                   (128, 28672, 8192), (2048, 4096, 4096), (1, 256, 512),
+                                   (37, 1024, 1024)])
 @pytest.mark.parametrize("scale_mult", [1.0, 8.0, 1.0 / 256])
 def test_quantized_output_matches_gemm_then_quantize(plugins, M, N, K, scale_mult):
     A, B = _operands(M, N, K, M + N + K)

@@ -23,7 +23,7 @@ def _case(plugins, M, I, K, seed):
 
 
 @pytest.mark.parametrize("M,I,K", [(96, 384, 512), (512, 1024, 1024), (300, 128, 768),
-                                   (1024, 28672, 8192)])
+                                   (1024, 28672, 8192), (3, 256, 512), (70, 640, 1024)])
 def test_swiglu_matches_torch_on_gemm_output(plugins, M, I, K):
     x, x_sf, w, w_sf, scale = _case(plugins, M, I, K, M + I + K)
     D = plugins.gemm_nvfp4(x, w, x_sf, w_sf, scale)
