@@ -90,7 +90,8 @@ struct Cfg {
   static constexpr int CTAS = PAIR ? 2 : 1;
   static constexpr int TILE_M = kRowsPerCta * CTAS;        // output rows per tile
   static constexpr int B_ROWS = BN / CTAS;                 // B rows each CTA loads
-  static_assert(BN % 128 == 0 && BN <= 256, "BN must be 128 or 256");
+  static_assert(BN == 256 || (!PAIR && (BN == 32 || BN == 64 || BN == 128)),
+                "BN must be 256, or 32/64/128 for the single-CTA form");
 
   static constexpr int A_STAGE = kRowsPerCta * kBKBytes;   // 16 KiB
   static constexpr int B_STAGE = B_ROWS * kBKBytes;
@@ -112,8 +113,10 @@ struct Cfg {
 
   // Tensor memory columns: accumulators, then one scale-factor slot per pipeline stage, so the
   // factors of later fills are written while the MMAs of earlier ones still read theirs. Within
-  // a slot: B's factors for K-steps 0..3 (BN/32 columns each), then A's (4 columns each).
-  static constexpr uint32_t SFB_COLS_PER_STEP = BN / 32;
+  // a slot: B's factors for K-steps 0..3 (BN/32 columns each, padded to 8 so that every step's
+  // address stays 8-column aligned), then A's (4 columns each).
+  static constexpr uint32_t SFB_COLS_PER_STEP = 8;
+  static constexpr uint32_t SFB_PART = kKSteps * SFB_COLS_PER_STEP;
   static constexpr uint32_t SF_SLOT_COLS = kKSteps * (4 + SFB_COLS_PER_STEP);
   static constexpr uint32_t COL_SF = BN * ACC_STAGES;
   static constexpr uint32_t COLS_USED = COL_SF + STAGES * SF_SLOT_COLS;
@@ -178,24 +181,23 @@ template <class C>
 __device__ __forceinline__ void write_sf_slot(uint32_t slot, uint32_t sfa_s, uint32_t sfb_s, int c,
                                               int q, int lane) {
   constexpr int kChunksB = C::BN / 32;
-  uint32_t vb[C::BN / 8];
+  constexpr int kStep = int(C::SFB_COLS_PER_STEP);
+  uint32_t vb[C::SFB_PART];
+#pragma unroll
+  for (int i = 0; i < int(C::SFB_PART); ++i) vb[i] = 0u;  // padding columns (BN < 256)
 #pragma unroll
   for (int i = 0; i < kChunksB; ++i) {
     const uint4 w = ptx::ld_shared_v4(sf_chunk_addr<C>(sfb_s, 32 * i + lane, c));
-    vb[0 * kChunksB + i] = w.x;
-    vb[1 * kChunksB + i] = w.y;
-    vb[2 * kChunksB + i] = w.z;
-    vb[3 * kChunksB + i] = w.w;
+    vb[0 * kStep + i] = w.x;
+    vb[1 * kStep + i] = w.y;
+    vb[2 * kStep + i] = w.z;
+    vb[3 * kStep + i] = w.w;
   }
   const uint4 a = ptx::ld_shared_v4(sf_chunk_addr<C>(sfa_s, 32 * q + lane, c));
-  if constexpr (C::BN == 256) {
-    ptx::tmem_st_32x32b_x32(slot, vb);
-  } else {
-    ptx::tmem_st_32x32b_x16(slot, vb);
-  }
-  // A: quarter q's MMA reads K-step j's factors from column BN/8 + 4j + q only; the other three
-  // columns of each group belong to the other quarters' lanes and are left alone.
-  const uint32_t sfa = slot + C::BN / 8 + uint32_t(q);
+  ptx::tmem_st_32x32b_x32(slot, vb);
+  // A: quarter q's MMA reads K-step j's factors from column SFB_PART + 4j + q only; the other
+  // three columns of each group belong to the other quarters' lanes and are left alone.
+  const uint32_t sfa = slot + C::SFB_PART + uint32_t(q);
   ptx::tmem_st_32x32b_x1(sfa + 0, a.x);
   ptx::tmem_st_32x32b_x1(sfa + 4, a.y);
   ptx::tmem_st_32x32b_x1(sfa + 8, a.z);
@@ -242,6 +244,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
             const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
             const __grid_constant__ DstMaps<NDST> dst, const Params p) {
   constexpr bool kPair = C::PAIR;
+  static_assert(MODE == kEpiBf16 || C::BN == 256, "epilogue variants use 256-column tiles");
   constexpr int kGroup = C::CTAS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -411,21 +414,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
           const uint64_t a_desc = a_desc0 + uint32_t(stage) * kADescStep;
           const uint64_t b_desc = b_desc0 + uint32_t(stage) * kBDescStep;
           const uint32_t t_sfb = t_sf0 + uint32_t(stage) * C::SF_SLOT_COLS;
-          const uint32_t t_sfa = t_sfb + C::BN / 8;
+          const uint32_t t_sfa = t_sfb + C::SFB_PART;
           // K-step j starts 32 bytes (2 descriptor units) further along the swizzled rows.
           if constexpr (kPair) {
             ptx::tc_mma_mxf4nvf4_pair(d_tmem, a_desc, b_desc, idesc, t_sfa, t_sfb, kb != 0 ? 1u : 0u);
 #pragma unroll
             for (int j = 1; j < kKSteps; ++j)
               ptx::tc_mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * j, b_desc + 2 * j, idesc, t_sfa + 4 * j,
-                                        t_sfb + j * (C::BN / 32), 1u);
+                                        t_sfb + j * C::SFB_COLS_PER_STEP, 1u);
             ptx::tc_commit_pair(&empty_bar[stage], 0x3);  // stage free in both CTAs
           } else {
             ptx::tc_mma_mxf4nvf4(d_tmem, a_desc, b_desc, idesc, t_sfa, t_sfb, kb != 0 ? 1u : 0u);
 #pragma unroll
             for (int j = 1; j < kKSteps; ++j)
               ptx::tc_mma_mxf4nvf4(d_tmem, a_desc + 2 * j, b_desc + 2 * j, idesc, t_sfa + 4 * j,
-                                   t_sfb + j * (C::BN / 32), 1u);
+                                   t_sfb + j * C::SFB_COLS_PER_STEP, 1u);
             ptx::tc_commit(&empty_bar[stage]);
           }
           if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
@@ -528,6 +531,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
           pk[g * 32 + i] = ptx::scaled_f32x2_to_bf16x2(r0[2 * i], r0[2 * i + 1], alpha2);
           pk[g * 32 + 16 + i] = ptx::scaled_f32x2_to_bf16x2(r1[2 * i], r1[2 * i + 1], alpha2);
         }
+      }
+      if constexpr (C::BN == 32) {  // one 32-column chunk
+        uint32_t r0[32];
+        ptx::tmem_ld_32x32b_x32(t_row, r0);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pk[i] = ptx::scaled_f32x2_to_bf16x2(r0[2 * i], r0[2 * i + 1], alpha2);
       }
       ptx::tc_fence_before_sync();
       __syncwarp();
@@ -756,6 +767,13 @@ using CfgSingle = Cfg<256, 4, 1, false, 1, 4>;
 // per shared-memory slot (64-byte rows, 2 slots), one 32 x 64 staging box per epilogue warp;
 // tensor memory 256 + 5 x 48 columns.
 using CfgPair = Cfg<256, 5, 1, true, 4, 2, 64, 1>;
+// Narrower single-CTA tiles for N too small to give half the SMs a 256-column tile (decode
+// shapes sharded along N: 28672 / 8 ranks = 14 tiles). More, narrower tiles put more SMs on the
+// weight stream; the ring is deeper (A/B stages are smaller) to keep enough bytes in flight per
+// SM. Each output element is still one chain of MMAs over K in the same order.
+using CfgSingle128 = Cfg<128, 6, 1, false, 1, 4>;
+using CfgSingle64 = Cfg<64, 8, 1, false, 1, 4>;
+using CfgSingle32 = Cfg<32, 10, 1, false, 1, 4>;
 
 // D of this launch: `count` destinations, each [M, N] with its own base and row pitch.
 struct DstDesc {
@@ -884,6 +902,16 @@ int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const 
   // A CTA pair covers 256 rows; for M <= 128 a single CTA per tile wastes no tensor work.
   if (M > kRowsPerCta)
     return launch<CfgPair, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+  // The widest single-CTA tile that still gives at least half the SMs a tile.
+  const int sms = current_device_sm_count(nullptr);
+  const auto tiles = [N](int64_t bn) { return (N + bn - 1) / bn; };
+  if (sms > 0 && 2 * tiles(256) <= sms) {
+    if (2 * tiles(128) > sms)
+      return launch<CfgSingle128, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+    if (2 * tiles(64) > sms)
+      return launch<CfgSingle64, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+    return launch<CfgSingle32, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+  }
   return launch<CfgSingle, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
 }
 

@@ -198,6 +198,22 @@ def test_gemm_allgather_on_one_gpu_matches_gemm(M, N, K):
             assert np.array_equal(got, full), f"world {world}: output of rank {i} differs"
 
 
+@pytest.mark.parametrize("M", [16, 128])
+def test_gemm_narrow_tiles_of_sharded_decode_bit_identical(plugins, M):
+    """A decode-shape weight split into 2, 4 or 8 column shards leaves too few 256-column tiles
+    per shard, so the shards run with 128-, 64- and 32-column tiles; every output element is
+    still the same MMA chain over K, so the shards reproduce the unsharded product bit for bit."""
+    rng = np.random.default_rng(M + 11)
+    N, K = 28672, 2048
+    A, B, Asf, Bsf = random_operands(rng, M, N, K)
+    full = plugins_gemm(plugins, A, B, Asf, Bsf, 0.75)
+    for P in (2, 4, 8):
+        w = N // P
+        parts = [plugins_gemm(plugins, A, B[r * w:(r + 1) * w], Asf, Bsf[r * w:(r + 1) * w], 0.75)
+                 for r in range(P)]
+        assert np.array_equal(np.concatenate(parts, axis=1), full), f"P={P}"
+
+
 def test_gemm_deterministic(plugins):
     rng = np.random.default_rng(9)
     A, B, Asf, Bsf = random_operands(rng, 1000, 1024, 4096)
