@@ -71,7 +71,9 @@ def parse_args():
     ap.add_argument("--workload", choices=["square", "decode", "prefill"], default="square",
                     help="square: 8192^3 (headline); decode: M x 28672 x 8192; "
                          "prefill: 16384 x 57344 x 8192 (N sharded across ranks)")
-    ap.add_argument("--m", type=int, default=128, help="decode tokens (16, 32, 64, 128)")
+    ap.add_argument("--tokens", "--m", dest="m", type=int, default=128,
+                    help="decode tokens (16, 32, 64, 128); under torchrun use --tokens, whose "
+                         "launcher would take --m for an abbreviation of its own options")
     ap.add_argument("--gather", action="store_true",
                     help="prefill/decode: include the chunked NCCL all-gather of D in the timing")
     ap.add_argument("--swiglu", action="store_true",
