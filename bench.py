@@ -2,21 +2,28 @@
 """bench.py — NVFP4 GEMM throughput on B200, one process per GPU.
 
 Headline: TFLOP/s of the block-scaled NVFP4 GEMM on the square workload M = N = K = 8192
-(A, B bf16 N(0,1), seed 2, quantized on the GPU with the reference recipe), at 1..8 GPUs.
-N > 1 is column-parallel (weak scaling): every rank owns an 8192-column shard of a global
-M x (8192*P) x K product (its own slice of B and B's scale factors, A replicated), with no
-data-path collective; `value` is the work of all ranks over the max-over-ranks device time.
+(A, B bf16 N(0,1) drawn on the host from seed 2, quantized on the GPU with the reference
+recipe), at 1..8 GPUs. N > 1 is column-parallel (weak scaling): every rank owns an 8192-column
+shard of a global M x (8192*P) x K product (its own slice of B and B's scale factors, A
+replicated), with no data-path collective; `value` is the work of all ranks over the
+max-over-ranks device time.
 
 One JSON line on rank 0. Besides the contract keys it carries:
-  roofline      the GEMM kernel against the FP4 dense peak (4 x the measured cuBLAS bf16 rate)
-  cpu_baseline  the CPU oracle port (dequantize + fp32 matmul) on a bounded row sample
+  roofline      the GEMM kernel against B200's dense FP4 peak, 9.0 PFLOP/s (`frac`); the
+                fraction of 4 x the measured cuBLAS bf16 rate is a secondary key
+  cpu_baseline  the CPU oracle port (dequantize + fp32 matmul) on the same full 8192^3 problem
   e2e           the same metric through my_plugins.gemm_nvfp4 with pinned host buffers,
                 host->device copies of the operands and device->host copy of D in the timing
   quantize / dequantize   GB/s of the 8192x8192 activation workload (0.5% x50 outliers)
+  prefill       16384 x 57344 x 8192, weight sharded along N over the ranks (strong scaling):
+                GEMM alone, GEMM with the all-gather fused into its epilogue, GEMM + NCCL
+                all-gather (N > 1), each with its per-rank roofline fraction
+  decode        M x 28672 x 8192 for M = 16 and 128, weight sharded along N: us per step
   clocks        SM clock samples (nvidia-smi) from warm-up start to the end of timing
 
 `--impl reference` times the CPU implementation of the reference arithmetic (the oracle port;
-the reference ships no CPU code and its GEMM does not build for sm_100a) on rank 0.
+the reference ships no CPU code and its GEMM does not build for sm_100a) on rank 0, on the
+same operands and config.
 """
 from __future__ import annotations
 
@@ -35,7 +42,8 @@ M_SQ = N_SQ = K_SQ = 8192
 L2_FLUSH_BYTES = 256 << 20          # > 126 MB L2
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
-NOMINAL_FP4_TFLOPS = 9000.0
+NOMINAL_FP4_TFLOPS = 9000.0        # B200 dense FP4 (the 18 PF HGX figure is with 2:4 sparsity)
+NVLINK_GBS = 770.0                 # measured peer copy rate per direction per GPU on this pool
 QUANT_BYTES = 8192 * 8192 * 2 + 8192 * 4096 + 8192 * 512   # 171,966,464 per pass
 
 
@@ -67,6 +75,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-quant", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="square workload: skip the prefill and decode measurements")
     ap.add_argument("--size", type=int, default=8192, help="M = N = K (profiling of small cases)")
     ap.add_argument("--workload", choices=["square", "decode", "prefill"], default="square",
                     help="square: 8192^3 (headline); decode: M x 28672 x 8192; "
@@ -196,19 +206,41 @@ def max_over_ranks(torch, world, value):
     return float(t.item())
 
 
+def square_inputs_host(size, rank=0):
+    """bf16 bit patterns (numpy uint16) of the square workload: A then B from one N(0,1) stream
+    seeded with 2; rank r > 0 of a weak-scaled run draws its own B shard from seed (2, r). Both
+    arms (and the CPU baseline) use exactly these operands."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import nvfp4_cases as cases
+    rng = np.random.default_rng(2)
+    A = cases.activation(rng, size, size)
+    B = cases.activation(rng if rank == 0 else np.random.default_rng([2, rank]), size, size)
+    return A, B
+
+
 def make_square_operands(torch, plugins, size, rank):
-    """A (replicated, seed 2) and this rank's B shard (seed 2 + rank) quantized on the GPU."""
-    g = torch.Generator(device="cuda").manual_seed(2)
-    A = torch.randn(size, size, device="cuda", generator=g).to(torch.bfloat16)
-    if rank > 0:
-        g = torch.Generator(device="cuda").manual_seed(2 + rank)
-    B = torch.randn(size, size, device="cuda", generator=g).to(torch.bfloat16)
+    """A (replicated) and this rank's B shard uploaded and quantized on the GPU with the
+    reference recipe s = 6*448 / amax."""
+    import numpy as np
+    A_bits, B_bits = square_inputs_host(size, rank)
+    A = torch.from_numpy(A_bits.view(np.int16)).cuda().view(torch.bfloat16)
+    B = torch.from_numpy(B_bits.view(np.int16)).cuda().view(torch.bfloat16)
     sA = 6 * 448 / A.abs().max().to(dtype=torch.float32)
     sB = 6 * 448 / B.abs().max().to(dtype=torch.float32)
     a, a_sf = plugins.quantize_nvfp4(A, sA)
     b, b_sf = plugins.quantize_nvfp4(B, sB)
     del A, B
     return a, b, a_sf, b_sf, (sA * sB).reshape(())
+
+
+def square_config(size, world):
+    """`config` of the square workload, the same for both arms."""
+    return {"workload": f"square_gemm_{size}", "M": size, "N": size * world, "K": size,
+            "n_per_rank": size, "parallelism": f"column-parallel N x{world}",
+            "l2": "GPU arm: flushed (256 MiB write) before every timed launch",
+            "inputs": "bf16 N(0,1), host numpy stream of seed 2 (A, then B; rank r>0 B from "
+                      "seed (2, r)), quantized with s = 6*448/amax"}
 
 
 def time_device(torch, fn, steps, warmup, flush, world):
@@ -249,40 +281,48 @@ def time_device_streaming(torch, fn, steps, warmup, world):
     return max_over_ranks(torch, world, s.elapsed_time(e))
 
 
-def cpu_baseline_gemm(a, b, a_sf, b_sf, scale, rows=256, budget_s=10.0):
-    """Oracle port of the reference arithmetic on the host: decode the block-scaled operands,
-    fp32 matmul (torch, all host threads), / scale, bf16. Bounded sample: `rows` rows of A."""
+def cpu_gemm_timer(qa, fa, qb, fb, scale):
+    """One step of the reference arithmetic on the host (the oracle port): decode both
+    block-scaled operands (oracle, OpenMP), fp32 matmul (torch, all host threads), / scale,
+    bf16. `rows` limits the step to the first rows of A (the full problem when None)."""
     import numpy as np
     import torch
     from oracle import oracle as O
-    A = a[:rows].cpu().numpy()
-    Asf = a_sf[:rows].view(torch.uint8).cpu().numpy()
-    B = b.cpu().numpy()
-    Bsf = b_sf.view(torch.uint8).cpu().numpy()
-    s = np.float32(scale.item())
+    s = torch.tensor(np.float32(scale))
+
+    def step(rows=None):
+        r = qa.shape[0] if rows is None else rows
+        da = torch.from_numpy(O.decode_scaled(qa[:r], fa[:r]))
+        db = torch.from_numpy(O.decode_scaled(qb, fb))
+        return ((da @ db.T) / s).to(torch.bfloat16)
+    return step
+
+
+def cpu_baseline_gemm(a, b, a_sf, b_sf, scale, runs=3):
+    """The CPU baseline of the GPU arm: the full problem, median of `runs` steps after one
+    untimed step."""
+    import torch
+    from oracle import oracle as O
+    step = cpu_gemm_timer(a.cpu().numpy(), a_sf.view(torch.uint8).cpu().numpy(), b.cpu().numpy(),
+                          b_sf.view(torch.uint8).cpu().numpy(), scale.item())
+    step()
     times = []
-    t_end = time.perf_counter() + budget_s
-    while True:
+    for _ in range(runs):
         t0 = time.perf_counter()
-        fa = torch.from_numpy(O.decode_scaled(A, Asf))
-        fb = torch.from_numpy(O.decode_scaled(B, Bsf))
-        d = (fa @ fb.T) / torch.tensor(s)
-        d = d.to(torch.bfloat16)
+        step()
         times.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end or len(times) >= 5:
-            break
     t = statistics.median(times)
-    flops = 2.0 * rows * B.shape[0] * A.shape[1] * 2
-    return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+    M, N, K = a.shape[0], b.shape[0], a.shape[1] * 2
+    return {"value": 2.0 * M * N * K / t / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
             "kind": "port",
-            "sample": f"{rows} of {a.shape[0]} rows of A x full B ({B.shape[0]}x{A.shape[1]*2}); "
-                      f"median of {len(times)} runs; oracle decode (OpenMP, {O.num_threads()} "
-                      f"threads) + torch fp32 matmul; os.cpu_count()={os.cpu_count()}"}
+            "sample": f"the full {M}x{N}x{K} problem (same operands as the GPU arm) per run, median "
+                      f"of {runs} runs after one untimed: oracle decode (OpenMP, {O.num_threads()} "
+                      f"threads) + torch fp32 matmul + / scale + bf16; os.cpu_count()={os.cpu_count()}"}
 
 
 def run_reference_arm(args):
-    """CPU implementation of the reference arithmetic on the same workload (rank 0 only)."""
-    import numpy as np
+    """CPU implementation of the reference arithmetic on the same operands and config as the
+    GPU arm (rank 0 only; other ranks exit without work)."""
     import torch
     from oracle import oracle as O
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -290,40 +330,42 @@ def run_reference_arm(args):
     if rank != 0:
         return 0
     size = args.size
-    rows = 128
-    rng = np.random.default_rng(2)
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
-    import nvfp4_cases as cases
-    Ab = cases.activation(rng, rows, size)
-    Bb = cases.activation(rng, size, size)
-    sA, sB = O.global_scale(Ab), O.global_scale(Bb)
+    A_bits, B_bits = square_inputs_host(size, 0)
+    sA, sB = O.global_scale(A_bits), O.global_scale(B_bits)
+    qa, fa = O.quantize(A_bits, sA)            # operands quantized once, as on the GPU arm
+    qb, fb = O.quantize(B_bits, sB)
+    del A_bits, B_bits
+    import numpy as np
+    step = cpu_gemm_timer(qa, fa, qb, fb, np.float32(sA) * np.float32(sB))
 
-    qa, fa = O.quantize(Ab, sA)            # operands quantized once, as on the GPU arm
-    qb, fb = O.quantize(Bb, sB)
-    scale = torch.tensor(np.float32(sA) * np.float32(sB))
-
-    def step():
-        da = torch.from_numpy(O.decode_scaled(qa, fa))
-        db = torch.from_numpy(O.decode_scaled(qb, fb))
-        return ((da @ db.T) / scale).to(torch.bfloat16)
-
-    for _ in range(max(args.warmup, 1)):
-        step()
+    # Each step is the full problem unless the requested steps would then run for more than
+    # ~3 minutes; then each step covers the first `rows` rows of A (a bounded sample of the same
+    # workload) so that the whole run still ends within a few minutes.
+    t0 = time.perf_counter()
+    step()
+    t_full = time.perf_counter() - t0
+    rows = size
+    n_more = max(args.warmup - 1, 0) + args.steps
+    if n_more * t_full > 180.0:
+        rows = max(128, min(size, int(size * 180.0 / (n_more * t_full)) // 128 * 128))
+    for _ in range(max(args.warmup - 1, 0)):
+        step(rows)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
-    dt = (time.perf_counter() - t0) / args.steps
-    flops = 2.0 * rows * size * size
-    val = flops / dt / 1e12
+        step(rows)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    val = 2.0 * rows * size * size / dt / 1e12
     cores = torch.get_num_threads()
-    sample = (f"{rows} of {size} rows of A x full B ({size}x{size}) per step: decode of the "
-              f"block-scaled operands (oracle, OpenMP {O.num_threads()} threads) + torch fp32 "
-              f"matmul + / scale + bf16")
+    sample = ((f"the full {size}x{size}x{size} problem per step" if rows == size else
+               f"{rows} of {size} rows of A x full B per step (the full problem took "
+               f"{t_full:.1f} s; steps bounded to ~3 min)")
+              + f": decode of the block-scaled operands (oracle, OpenMP {O.num_threads()} threads) "
+                "+ torch fp32 matmul + / scale + bf16, operands identical to the GPU arm's")
     line = {"metric": "nvfp4_gemm_tflops", "value": val, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/ue4m3->f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"square_gemm_{size}", "M": size, "N": size, "K": size},
+            "config": square_config(size, world),
             "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -341,7 +383,7 @@ def run_ours(args):
     M = N = K = size
     flops = 2.0 * M * N * K
     hbm_gbs, bf16_tf, peak_src = measured_peaks()
-    fp4_peak = 4.0 * bf16_tf
+    fp4_peak_bf16 = 4.0 * bf16_tf
 
     a, b, a_sf, b_sf, scale = make_square_operands(torch, plugins, size, rank)
     d = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
@@ -368,14 +410,15 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "e2m1/ue4m3->f32",
         "data": "synthetic",
-        "config": {"workload": f"square_gemm_{size}", "M": M, "N": N * world, "K": K,
-                   "n_per_rank": N, "parallelism": f"column-parallel N x{world}",
-                   "l2": "flushed (256 MiB write) before every timed launch",
-                   "inputs": "bf16 N(0,1) seed 2 (B shard seed 2+rank), quantized on device"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp4_peak,
-                     "unit": "TFLOP/s", "frac": achieved / fp4_peak, "traffic": traffic,
-                     "peak_source": f"4 x {peak_src} cuBLAS bf16 burst ({bf16_tf:.1f} TF/s)",
-                     "frac_of_nominal_9000": achieved / NOMINAL_FP4_TFLOPS,
+        "config": square_config(size, world),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": NOMINAL_FP4_TFLOPS,
+                     "unit": "TFLOP/s", "frac": achieved / NOMINAL_FP4_TFLOPS, "traffic": traffic,
+                     "peak_source": "B200 dense FP4 tensor peak, 9.0 PFLOP/s (nominal; "
+                                    "MEASURED_PEAKS.json holds no FP4 figure)",
+                     "peak_4x_measured_bf16": fp4_peak_bf16,
+                     "frac_of_4x_measured_bf16": achieved / fp4_peak_bf16,
+                     "peak_4x_measured_bf16_source": f"4 x {peak_src} cuBLAS bf16 burst "
+                                                     f"({bf16_tf:.1f} TF/s)",
                      "kernel": "nvfp4::gemm::gemm_kernel (tcgen05 mxf4nvf4)"},
         "gpu_launches": args.steps,
         "clocks": clocks,
@@ -540,6 +583,13 @@ def run_ours(args):
                               "consecutive steps on two streams (copies overlap across steps)"}
         line["gpu_launches"] += e2e_steps
 
+    # ---- the sharded workloads at this N (prefill and decode, weight sharded along N)
+    if not args.no_sharded and size == 8192:
+        summary, n_launch = sharded_summary(torch, plugins, capi, world, rank, args.steps,
+                                            args.warmup, flush, stream_h, hbm_gbs)
+        line.update(summary)
+        line["gpu_launches"] += n_launch
+
     # ---- CPU baseline (rank 0, N = 1 only)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_gemm(a, b, a_sf, b_sf, scale)
@@ -556,23 +606,21 @@ def run_ours(args):
     return 0
 
 
-def run_sharded_workload(args):
-    """decode / prefill: a fixed global problem (strong scaling) whose weight is sharded
-    column-parallel across the ranks; A is replicated. Optionally times the chunked NCCL
-    all-gather of D together with the GEMM."""
-    import torch
-    from my_nvfp4_gemm_b200 import capi, load_my_plugins, sharded
-    plugins = load_my_plugins()
-    world, rank, local = dist_setup(torch)
+def sharded_inputs(torch, plugins, workload, m, world, rank, swiglu=False, keep_bf16=False):
+    """Operands of the sharded workloads, drawn on the GPU.
+
+    prefill: A 16384 x 8192 bf16 N(0,1) with 0.5% of the elements x50 (seed 4), weight
+             57344 x 8192 N(0, 0.02^2) (seed 1004);
+    decode:  A m x 8192 N(0,1) (seed 3), weight 28672 x 8192 N(0, 0.02^2) (seed 1003).
+    The weight's global scale is taken over the whole weight; this rank quantizes its column
+    shard (rows [n0, n1) of the weight). With swiglu the weight is gate+up (rows [gate; up]),
+    interleaved in groups of 128 rows before sharding into whole 256-row groups."""
+    from my_nvfp4_gemm_b200 import sharded
     K = 8192
-    if args.workload == "decode":
-        M, N, seed, frac, name = args.m, 28672, 3, 0.0, f"decode_m{args.m}_n28672_k8192"
+    if workload == "decode":
+        M, N, seed, frac, name = m, 28672, 3, 0.0, f"decode_m{m}_n28672_k8192"
     else:
         M, N, seed, frac, name = 16384, 57344, 4, 0.005, "prefill_16384x57344x8192"
-    swiglu = bool(args.swiglu and args.workload == "prefill")
-    if swiglu and args.gather:
-        raise SystemExit("--swiglu and --gather are separate measurements")
-    # SwiGLU keeps each rank's gate/up row pairs together: shards of whole 256-row groups
     n0, n1 = sharded.shard_range(N, world, rank, align=256 if swiglu else 128)
     g = torch.Generator(device="cuda").manual_seed(seed)
     X = torch.randn(M, K, device="cuda", generator=g)
@@ -582,8 +630,6 @@ def run_sharded_workload(args):
     X = X.to(torch.bfloat16)
     sX = (6 * 448 / X.abs().max().to(torch.float32)).reshape(())
     x, x_sf = plugins.quantize_nvfp4(X, sX)
-    del X
-    # the weight: quantized shard by shard (N(0, 0.02^2)), global scale over the whole weight
     gw = torch.Generator(device="cuda").manual_seed(seed + 1000)
     W = (torch.randn(N, K, device="cuda", generator=gw) * 0.02).to(torch.bfloat16)
     sW = (6 * 448 / W.abs().max().to(torch.float32)).reshape(())
@@ -597,100 +643,183 @@ def run_sharded_workload(args):
         del wq, wq_sf, wi, wi_sf
     else:
         w, w_sf = plugins.quantize_nvfp4(W[n0:n1].contiguous(), sW)
-    del W
-    torch.cuda.empty_cache()
-    scale = (sX * sW).reshape(())
-    n_loc = n1 - n0
-    d = torch.empty(M, n_loc, dtype=torch.bfloat16, device="cuda")
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
-    stream_h = torch.cuda.current_stream().cuda_stream
-    ptrs = (x.data_ptr(), w.data_ptr(), x_sf.data_ptr(), w_sf.data_ptr(), scale.data_ptr(), d.data_ptr())
+    out = dict(x=x, x_sf=x_sf, w=w, w_sf=w_sf, scale=(sX * sW).reshape(()), sX=sX, sW=sW,
+               M=M, N=N, K=K, n0=n0, n1=n1, n_loc=n1 - n0, name=name)
+    if keep_bf16:
+        out.update(X=X, W=W)
+    else:
+        del X, W
+        torch.cuda.empty_cache()
+    return out
 
-    fused = bool(args.gather and args.fused_gather and world > 1)
-    if swiglu:
+
+def sharded_step(torch, capi, sharded, inp, mode, stream_h):
+    """One step of a sharded workload on this rank. mode: "gemm" (this rank's shard of D),
+    "fused" (GEMM with the all-gather fused into the epilogue), "nccl" (GEMM per chunk of rows,
+    each chunk's NCCL all-gather overlapping the next chunk), "swiglu" (gate+up GEMM with
+    SwiGLU in the epilogue), "rotate" (decode: consecutive calls read copies of the weight in
+    rotation, together > 3 x L2, as the layers of a decode step stream different weights)."""
+    x, x_sf, w, w_sf, scale = inp["x"], inp["x_sf"], inp["w"], inp["w_sf"], inp["scale"]
+    M, K, n_loc = inp["M"], inp["K"], inp["n_loc"]
+    if mode == "fused" or mode == "nccl":
+        def step():
+            sharded.gemm_column_parallel(x, w, x_sf, w_sf, scale, gather=True, chunks=4,
+                                         fused=(mode == "fused"))
+        return step
+    if mode == "swiglu":
         out = torch.empty(M, n_loc // 2, dtype=torch.bfloat16, device="cuda")
 
         def step():
-            st = capi.gemm_swiglu(x.data_ptr(), w.data_ptr(), x_sf.data_ptr(), w_sf.data_ptr(),
-                                  scale.data_ptr(), out.data_ptr(), M, n_loc, K, stream_h)
-            if st:
-                raise capi.NvFp4Error(st, "nvfp4_gemm_swiglu")
-    elif args.gather and world > 1:
-        def step():
-            sharded.gemm_column_parallel(x, w, x_sf, w_sf, scale, gather=True, chunks=4,
-                                         fused=fused)
-    else:
-        def step():
-            st = capi.gemm(*ptrs, M, n_loc, K, stream_h)
-            if st:
-                raise capi.NvFp4Error(st, "nvfp4_gemm")
-
-    # decode: consecutive calls stream different weights, as the layers of a decode step do.
-    # Copies of the weight shard (together > 3 x L2) are used in rotation and the calls run back
-    # to back, so each reads its weight from HBM with no flush in between (a flush by writing
-    # leaves L2 full of dirty lines whose write-back the next call would pay for).
-    rotate = args.workload == "decode" and not args.gather
-    n_copies = 0
-    if rotate:
-        import itertools
+            capi.check(capi.gemm_swiglu(x.data_ptr(), w.data_ptr(), x_sf.data_ptr(), w_sf.data_ptr(),
+                                        scale.data_ptr(), out.data_ptr(), M, n_loc, K, stream_h),
+                       "nvfp4_gemm_swiglu")
+        return step
+    d = torch.empty(M, n_loc, dtype=torch.bfloat16, device="cuda")
+    weights = [(w, w_sf)]
+    if mode == "rotate":
         per_copy = w.numel() + w_sf.numel()
         n_copies = max(2, -(-3 * (126 << 20) // per_copy))
-        copies = [(w, w_sf)] + [(w.clone(), w_sf.clone()) for _ in range(n_copies - 1)]
-        order = itertools.cycle(copies)
+        weights += [(w.clone(), w_sf.clone()) for _ in range(n_copies - 1)]
+        inp["n_copies"] = n_copies
+    turn = [0]
 
-        def step():
-            wc, wc_sf = next(order)
-            st = capi.gemm(x.data_ptr(), wc.data_ptr(), x_sf.data_ptr(), wc_sf.data_ptr(),
-                           scale.data_ptr(), d.data_ptr(), M, n_loc, K, stream_h)
-            if st:
-                raise capi.NvFp4Error(st, "nvfp4_gemm")
+    def step():
+        wc, wc_sf = weights[turn[0]]
+        turn[0] = (turn[0] + 1) % len(weights)
+        capi.check(capi.gemm(x.data_ptr(), wc.data_ptr(), x_sf.data_ptr(), wc_sf.data_ptr(),
+                             scale.data_ptr(), d.data_ptr(), M, n_loc, K, stream_h), "nvfp4_gemm")
+    return step
+
+
+def time_sharded(torch, step, mode, steps, warmup, flush, world):
+    """ms per step, max over ranks: decode rotation back to back, the rest L2-flushed."""
+    if mode == "rotate":
+        return time_device_streaming(torch, step, steps, warmup, world) / steps
+    return time_device(torch, step, steps, warmup, flush, world) / steps
+
+
+def sharded_roofline(inp, ms, world, hbm_gbs, gather=False):
+    """Per-rank roofline of a sharded step: FP4 tensor peak (prefill), HBM (decode), and with a
+    gather the slower of the tensor bound and this rank's output bytes over NVLink."""
+    M, K, n_loc = inp["M"], inp["K"], inp["n_loc"]
+    flops_rank = 2.0 * M * n_loc * K
+    bytes_rank = n_loc * K * (0.5 + 1 / 16) + M * K * (0.5 + 1 / 16) + 2.0 * M * n_loc
+    tf = flops_rank / (ms * 1e-3) / 1e12
+    gbs = bytes_rank / (ms * 1e-3) / 1e9
+    r = {"achieved_tflops_per_rank": tf, "frac_fp4_peak_per_rank": tf / NOMINAL_FP4_TFLOPS,
+         "achieved_gbs_per_rank": gbs, "frac_hbm_per_rank": gbs / hbm_gbs,
+         "algorithmic_bytes_per_rank": bytes_rank}
+    if gather:
+        nvlink_bytes = 2.0 * M * n_loc * (world - 1)
+        bound_ms = max(flops_rank / (NOMINAL_FP4_TFLOPS * 1e12), nvlink_bytes / (NVLINK_GBS * 1e9)) * 1e3
+        r.update(nvlink_bytes_out_per_rank=nvlink_bytes, bound_ms=bound_ms, frac_of_bound=bound_ms / ms)
+    return r
+
+
+def sharded_summary(torch, plugins, capi, world, rank, steps, warmup, flush, stream_h, hbm_gbs):
+    """The `prefill` and `decode` keys of the square line: the sharded workloads at this N."""
+    from my_nvfp4_gemm_b200 import sharded
+    out, launches = {}, 0
+    inp = sharded_inputs(torch, plugins, "prefill", 0, world, rank)
+    n_p = max(3, min(steps, 20))
+    pre = {"workload": inp["name"], "n_per_rank": inp["n_loc"], "steps": n_p,
+           "scaling": "strong", "l2": "flushed (256 MiB write) before every timed step"}
+    modes = ["gemm"] + (["fused", "nccl"] if world > 1 else [])
+    for mode in modes:
+        ms = time_sharded(torch, sharded_step(torch, capi, sharded, inp, mode, stream_h), mode,
+                          n_p, warmup, flush, world)
+        key = {"gemm": "gemm_only", "fused": "fused_all_gather", "nccl": "nccl_all_gather"}[mode]
+        pre[key] = {"ms_per_step": ms,
+                    "value": 2.0 * inp["M"] * inp["N"] * inp["K"] / (ms * 1e-3) / 1e12,
+                    "unit": "TFLOP/s",
+                    "roofline": sharded_roofline(inp, ms, world, hbm_gbs, gather=mode != "gemm")}
+        launches += (n_p + warmup) * (4 if mode == "nccl" else 1)
+    if world > 1:
+        sharded.release_peer_outputs()
+    out["prefill"] = pre
+    del inp
+    torch.cuda.empty_cache()
+    dec = {"workload": "decode_m{16,128}_n28672_k8192", "scaling": "strong",
+           "l2": "weight copies (> 3 x L2 together) in rotation, calls back to back"}
+    n_d = max(3, min(steps, 200))
+    for m in (16, 128):
+        inp = sharded_inputs(torch, plugins, "decode", m, world, rank)
+        ms = time_sharded(torch, sharded_step(torch, capi, sharded, inp, "rotate", stream_h),
+                          "rotate", n_d, warmup, flush, world)
+        dec[f"m{m}"] = {"us_per_step": ms * 1e3, "n_per_rank": inp["n_loc"], "steps": n_d,
+                        "roofline": sharded_roofline(inp, ms, world, hbm_gbs)}
+        launches += n_d + warmup
+        del inp
+        torch.cuda.empty_cache()
+    out["decode"] = dec
+    return out, launches
+
+
+def run_sharded_workload(args):
+    """decode / prefill: a fixed global problem (strong scaling) whose weight is sharded
+    column-parallel across the ranks; A is replicated. Optionally times the chunked NCCL
+    all-gather of D (or the all-gather fused into the GEMM's epilogue) with the GEMM."""
+    import torch
+    from my_nvfp4_gemm_b200 import capi, load_my_plugins, sharded
+    plugins = load_my_plugins()
+    world, rank, local = dist_setup(torch)
+    swiglu = bool(args.swiglu and args.workload == "prefill")
+    if swiglu and args.gather:
+        raise SystemExit("--swiglu and --gather are separate measurements")
+    inp = sharded_inputs(torch, plugins, args.workload, args.m, world, rank, swiglu=swiglu)
+    M, N, K, n_loc = inp["M"], inp["N"], inp["K"], inp["n_loc"]
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    stream_h = torch.cuda.current_stream().cuda_stream
+    fused = bool(args.gather and args.fused_gather and world > 1)
+    if swiglu:
+        mode = "swiglu"
+    elif args.gather and world > 1:
+        mode = "fused" if fused else "nccl"
+    elif args.workload == "decode":
+        mode = "rotate"
+    else:
+        mode = "gemm"
+    step = sharded_step(torch, capi, sharded, inp, mode, stream_h)
 
     hbm_gbs, bf16_tf, peak_src = measured_peaks()
     sampler = ClockSampler(gpu_uuid(torch, torch.cuda.current_device()))
     with sampler:
-        if rotate:
-            total = time_device_streaming(torch, step, args.steps, args.warmup, world)
-        else:
-            total = time_device(torch, step, args.steps, args.warmup, flush, world)
-    ms = total / args.steps
+        ms = time_sharded(torch, step, mode, args.steps, args.warmup, flush, world)
     flops = 2.0 * M * N * K
-    # algorithmic bytes of this rank's GEMM: its weight shard + scales, the activation, D shard
-    bytes_rank = n_loc * K * (0.5 + 1 / 16) + M * K * (0.5 + 1 / 16) + 2.0 * M * n_loc
-    achieved_tf = 2.0 * M * n_loc * K / (ms * 1e-3) / 1e12
-    achieved_gbs = bytes_rank / (ms * 1e-3) / 1e9
+    rl = sharded_roofline(inp, ms, world, hbm_gbs, gather=mode in ("fused", "nccl"))
+    decode = M <= 128
     line = {
         "metric": "nvfp4_gemm_tflops", "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "e2m1/ue4m3->f32", "data": "synthetic",
-        "config": {"workload": name, "M": M, "N": N, "K": K, "n_per_rank": n_loc,
+        "config": {"workload": inp["name"], "M": M, "N": N, "K": K, "n_per_rank": n_loc,
                    "parallelism": f"column-parallel N x{world}",
-                   "all_gather_in_timing": bool(args.gather and world > 1),
+                   "all_gather_in_timing": mode in ("fused", "nccl"),
                    "epilogue": ("SwiGLU (gate+up interleaved in 128-row groups), output "
                                 f"[M, {N // 2}]" if swiglu else "bf16 D"),
-                   "all_gather": ("fused into the GEMM epilogue (NVLink stores)" if fused else
-                                  "NCCL all_gather_into_tensor, 4 chunks" if args.gather and world > 1
+                   "all_gather": ("fused into the GEMM epilogue (NVLink stores)" if mode == "fused"
+                                  else "NCCL all_gather_into_tensor, 4 chunks" if mode == "nccl"
                                   else None),
-                   "l2": (f"{n_copies} copies of the weight shard in rotation, calls back to "
-                          "back: every call reads its weight from HBM" if rotate else
-                          "flushed (256 MiB write) before every timed step")},
-        "roofline": {"bound": "hbm" if M <= 128 else "tensor",
-                     "achieved": achieved_gbs if M <= 128 else achieved_tf,
-                     "peak": hbm_gbs if M <= 128 else 4 * bf16_tf,
-                     "unit": "GB/s" if M <= 128 else "TFLOP/s",
-                     "frac": (achieved_gbs / hbm_gbs) if M <= 128 else achieved_tf / (4 * bf16_tf),
-                     "achieved_tflops": achieved_tf, "frac_fp4_peak": achieved_tf / (4 * bf16_tf),
-                     "achieved_gbs": achieved_gbs, "frac_hbm": achieved_gbs / hbm_gbs,
-                     "algorithmic_bytes_per_rank": bytes_rank,
-                     "traffic": (profiled_traffic(f"gemm_decode_m{M}")
-                                 if args.workload == "decode" and world == 1 else None),
-                     "peak_source": f"{peak_src}: HBM {hbm_gbs} GB/s, FP4 4 x bf16 {bf16_tf} TF/s"},
-        "gpu_launches": args.steps * (1 if fused else 4 if (args.gather and world > 1) else 1),
+                   "l2": (f"{inp.get('n_copies')} copies of the weight shard in rotation, calls "
+                          "back to back: every call reads its weight from HBM" if mode == "rotate"
+                          else "flushed (256 MiB write) before every timed step")},
+        "roofline": dict({"bound": "hbm" if decode else "tensor",
+                          "achieved": rl["achieved_gbs_per_rank"] if decode else rl["achieved_tflops_per_rank"],
+                          "peak": hbm_gbs if decode else NOMINAL_FP4_TFLOPS,
+                          "unit": "GB/s" if decode else "TFLOP/s",
+                          "frac": rl["frac_hbm_per_rank"] if decode else rl["frac_fp4_peak_per_rank"],
+                          "traffic": (profiled_traffic(f"gemm_decode_m{M}")
+                                      if args.workload == "decode" and world == 1 else None),
+                          "peak_source": f"{peak_src} HBM {hbm_gbs} GB/s; FP4 dense 9.0 PFLOP/s "
+                                         "(nominal)"}, **rl),
+        "gpu_launches": args.steps * (4 if mode == "nccl" else 1),
         "clocks": sampler.summary(),
     }
     if swiglu and world == 1:
         # the unfused equivalent: bf16 D of the gate+up GEMM, then torch silu(g) * u
         import torch.nn.functional as F
+        x, x_sf, w, w_sf, scale = inp["x"], inp["x_sf"], inp["w"], inp["w_sf"], inp["scale"]
         d_full = torch.empty(M, n_loc, dtype=torch.bfloat16, device="cuda")
         half = n_loc // 2
 
@@ -701,17 +830,9 @@ def run_sharded_workload(args):
             (F.silu(d_full[:, :half].float()) * d_full[:, half:].float()).to(torch.bfloat16)
 
         n_u = max(3, min(args.steps, 10))
-        t_u = time_device(torch, unfused, n_u, args.warmup, flush, world) / n_u
-        line["gemm_then_torch_silu_mul_ms"] = t_u
+        line["gemm_then_torch_silu_mul_ms"] = time_device(torch, unfused, n_u, args.warmup, flush,
+                                                          world) / n_u
         del d_full
-    if args.gather and world > 1:
-        # roofline of the GEMM with its gather: the slower of the tensor bound and this rank's
-        # output bytes over NVLink (measured 770 GB/s per direction per GPU on this pool)
-        nvlink_bytes = 2.0 * M * n_loc * (world - 1)
-        bound_ms = max(2.0 * M * n_loc * K / (4 * bf16_tf * 1e12), nvlink_bytes / 770e9) * 1e3
-        line["roofline"]["gather"] = {"nvlink_bytes_out_per_rank": nvlink_bytes,
-                                      "bound_ms": bound_ms, "frac": bound_ms / ms,
-                                      "nvlink_gbs_per_direction": 770.0}
     if rank == 0:
         emit(line)
     if world > 1:

@@ -85,8 +85,9 @@ int nvfp4_quantize_auto_scale(const void* input, int64_t numel, void* output, vo
  * No counterpart in the reference. It allocates nothing: its scratch (partial maxima) is a fixed
  * 32 KiB device array inside this library, present on every GPU that loads it until the process
  * exits. Inputs are limited to numel <= 2^30 elements; larger calls return NVFP4_ERR_TOO_LARGE
- * before doing anything. The first call on a device looks up the array's device address (once
- * per device), so make that first call outside any stream capture. All calls on a device share
+ * before doing anything. Every call looks up the array's device address on the current device
+ * (so a cudaDeviceReset in between is harmless); the first lookup on a device may load the
+ * library's device code there, so make that first call outside any stream capture. All calls on a device share
  * the array: calls that overlap on the GPU (e.g. on two streams at once) race and must be
  * ordered by the caller. Results are identical to nvfp4_quantize_auto_scale.
  */

@@ -14,7 +14,6 @@
 // every warp store is 512 contiguous bytes; the scale is read from device memory so no host
 // synchronisation is needed.
 #include <cstdint>
-#include <mutex>
 
 #include "block_quant.cuh"
 #include "capi_util.h"
@@ -237,25 +236,17 @@ int launch_quantize_auto_scale(const void* input, int64_t numel, void* output, v
 // It is a fixed 32 KiB on every GPU that loads this library, until the process exits.
 constexpr int64_t kNoAllocMaxPartials = 8192;  // one per 128 Ki elements: inputs up to 2^30
 static __device__ __align__(256) uint32_t g_noalloc_amax_partials[kNoAllocMaxPartials];
-constexpr int kNoAllocMaxDevices = 64;
 
-// The array's name is only a stand-in in host code; its device address must be looked up with
-// the device current. Done once per device, on the first call there (which therefore should not
-// be inside a stream capture).
+// The array's name is only a stand-in in host code; its device address is looked up with the
+// current device, on every call: the address stays right even if the caller resets the device
+// (cudaDeviceReset rebuilds the context and may place the array elsewhere). The first lookup on
+// a device can load this library's device code there, so that first call should not be inside a
+// stream capture; later lookups allocate nothing and do not synchronise.
 int noalloc_partials(uint32_t** out) {
-  static std::once_flag flags[kNoAllocMaxDevices];
-  static uint32_t* addr[kNoAllocMaxDevices];
-  static cudaError_t errs[kNoAllocMaxDevices];
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
-    return NVFP4_ERR_NO_DEVICE;
-  std::call_once(flags[dev], [&] {
-    void* ptr = nullptr;
-    errs[dev] = cudaGetSymbolAddress(&ptr, g_noalloc_amax_partials);
-    addr[dev] = static_cast<uint32_t*>(ptr);
-  });
-  if (errs[dev] != cudaSuccess || addr[dev] == nullptr) return NVFP4_ERR_CUDA;
-  *out = addr[dev];
+  void* ptr = nullptr;
+  if (cudaGetSymbolAddress(&ptr, g_noalloc_amax_partials) != cudaSuccess || ptr == nullptr)
+    return NVFP4_ERR_CUDA;
+  *out = static_cast<uint32_t*>(ptr);
   return NVFP4_OK;
 }
 

@@ -95,13 +95,28 @@ class PeerOutput:
 
     def __init__(self, M: int, N: int, device: torch.device, group=None):
         from . import capi
+        self.group = group                  # held so the cache key's group stays alive
         self.world, self.rank = world_and_rank(group)
         self.local = torch.empty(M, N, dtype=torch.bfloat16, device=device)
-        handle, offset = capi.ipc_export(self.local.data_ptr())
+        # Every rank takes part in the exchange even when its own export failed, so that all
+        # ranks see the failure and raise together instead of some waiting in the collective.
+        try:
+            mine = (True,) + capi.ipc_export(self.local.data_ptr())
+        except capi.NvFp4Error as e:
+            mine = (False, str(e), 0)
         shared = [None] * self.world
-        dist.all_gather_object(shared, (handle, offset), group=group)
+        dist.all_gather_object(shared, mine, group=group)
+        failed = [r for r, (ok, _, _) in enumerate(shared) if not ok]
+        if failed:
+            raise RuntimeError(
+                f"fused all-gather: rank(s) {failed} could not export their output buffer for "
+                f"CUDA IPC ({shared[failed[0]][1]}). Legacy IPC handles need memory from "
+                "cudaMalloc; torch's allocator with PYTORCH_CUDA_ALLOC_CONF=expandable_segments:True "
+                "maps its segments with cuMemCreate/cuMemMap, which cannot be exported this way. "
+                "Unset expandable_segments, or call gemm_column_parallel(..., fused=False) for "
+                "the NCCL all-gather.")
         self.ptrs, self._opened = [], []
-        for r, (h, off) in enumerate(shared):
+        for r, (_, h, off) in enumerate(shared):
             if r == self.rank:
                 self.ptrs.append(self.local.data_ptr())
             else:
@@ -121,8 +136,14 @@ _peer_outputs: dict = {}
 
 
 def peer_output(M: int, N: int, device: torch.device, group=None) -> PeerOutput:
+    """The cached shared output of this shape for `group`. Each cached entry holds a reference
+    to its group, so the group's id cannot be reused by a new group while the entry exists; a
+    hit is also checked against the group's current world size and rank."""
     key = (M, N, str(device), id(group))
     po = _peer_outputs.get(key)
+    if po is not None and (po.group is not group or (po.world, po.rank) != world_and_rank(group)):
+        po.close()
+        po = None
     if po is None:
         po = _peer_outputs[key] = PeerOutput(M, N, device, group)
     return po

@@ -63,4 +63,6 @@ def main(out_path: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "gpurun_out", "ref_kernels_sm100a.npz"))
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <out.npz>")
+    main(sys.argv[1])

@@ -222,9 +222,10 @@ def test_gemm_deterministic(plugins):
         assert np.array_equal(plugins_gemm(plugins, A, B, Asf, Bsf, 1.0), first)
 
 
-def test_gemm_square_8192_sampled_rows(plugins, oracle):
+def test_gemm_square_8192_full_output(plugins, oracle):
     """The square workload: M = N = K = 8192 from bf16 N(0,1) (seed 2), quantized on the GPU.
-    Full-size output; 64 sampled rows checked against the oracle, plus the row-shard property."""
+    Every element of the 8192 x 8192 output is checked against the oracle (float64 sums), plus
+    the row-shard property on 64 sampled rows."""
     g = torch.Generator(device="cuda").manual_seed(2)
     A = torch.randn(8192, 8192, device="cuda", generator=g).to(torch.bfloat16)
     B = torch.randn(8192, 8192, device="cuda", generator=g).to(torch.bfloat16)
@@ -235,21 +236,22 @@ def test_gemm_square_8192_sampled_rows(plugins, oracle):
     del A, B
     scale = sA * sB
     d = plugins.gemm_nvfp4(a, b, a_sf, b_sf, scale)
-    rows = np.sort(np.random.default_rng(0).choice(8192, 64, replace=False))
     a_np, asf_np = a.cpu().numpy(), a_sf.view(torch.uint8).cpu().numpy()
     b_np, bsf_np = b.cpu().numpy(), b_sf.view(torch.uint8).cpu().numpy()
-    ref = oracle.gemm_f32(a_np[rows], b_np, asf_np[rows], bsf_np, scale.item())
-    out = d.view(torch.int16)[torch.from_numpy(rows).cuda()].cpu().numpy().view(np.uint16)
-    assert_gemm_close(out, ref, "8192^3 sampled rows")
+    ref = oracle.gemm_f32(a_np, b_np, asf_np, bsf_np, scale.item())
+    assert_gemm_close(d.view(torch.int16).cpu().numpy().view(np.uint16), ref, "8192^3 full output")
     # the same rows computed as a separate (small-M) problem are bit-identical
+    rows = np.sort(np.random.default_rng(0).choice(8192, 64, replace=False))
     idx = torch.from_numpy(rows).cuda()
     d_rows = plugins.gemm_nvfp4(a[idx].contiguous(), b, a_sf[idx].contiguous(), b_sf, scale)
     assert torch.equal(d_rows.view(torch.int16), d.view(torch.int16)[idx])
 
 
-@pytest.mark.parametrize("M", [16, 128])
+@pytest.mark.parametrize("M", [16, 32, 64, 128])
 def test_gemm_skinny_decode_shape(plugins, oracle, M):
-    """Decode-style shape M x 28672 x 8192: weight from N(0, 0.02^2), activations N(0,1), seed 3."""
+    """Decode-style shape M x 28672 x 8192 for every token count of the decode workload
+    (16, 32, 64, 128): weight from N(0, 0.02^2), activations N(0,1), seed 3. M < 128 runs the
+    single-CTA form whose A boxes cover only the M existing rows."""
     rng = np.random.default_rng(3)
     Wb = cases.activation(rng, 28672, 8192, std=0.02)
     Xb = cases.activation(rng, M, 8192)
@@ -263,6 +265,29 @@ def test_gemm_skinny_decode_shape(plugins, oracle, M):
     ref = oracle.gemm_f32(x.cpu().numpy(), w.cpu().numpy(), x_sf.view(torch.uint8).cpu().numpy(),
                           w_sf.view(torch.uint8).cpu().numpy(), scale)
     assert_gemm_close(d.view(torch.int16).cpu().numpy().view(np.uint16), ref, f"M={M} skinny")
+
+
+@pytest.mark.parametrize("M,N,K", [(5, 520, 1024), (16, 28672, 2048), (100, 1024, 512),
+                                   (130, 512, 512)])
+def test_gemm_leaves_memory_past_row_m_untouched(M, N, K):
+    """With M < 128 the single-CTA form still runs 128-row MMAs; shared-memory rows past M hold
+    stale bytes (which may decode as NaN scale factors) and their accumulator lanes must never
+    be stored. D is given as the first M rows of a larger buffer filled with a sentinel: the
+    rows past M keep the sentinel and the first M rows equal the plain call's output."""
+    rng = np.random.default_rng(M + N)
+    A, B, Asf, Bsf = random_operands(rng, M, N, K)
+    Asf[1::4, 3] = 0x7F                           # NaN scale bytes in some live rows too
+    full = capi_gemm(A, B, Asf, Bsf, 1.0)
+    a, b, asf, bsf = to_dev(A, B, Asf, Bsf)
+    big = torch.full((M + 130, N), 0x1357, dtype=torch.int16, device="cuda")
+    s = torch.tensor(1.0, dtype=torch.float32, device="cuda")
+    capi.check(capi.gemm(a.data_ptr(), b.data_ptr(), asf.data_ptr(), bsf.data_ptr(), s.data_ptr(),
+                         big.data_ptr(), M, N, K, torch.cuda.current_stream().cuda_stream),
+               "nvfp4_gemm")
+    torch.cuda.synchronize()
+    got = big.cpu().numpy().view(np.uint16)
+    assert (got[M:] == 0x1357).all(), "rows past M were written"
+    assert np.array_equal(got[:M], full)
 
 
 def test_gemm_k_zero_and_empty(plugins):

@@ -152,7 +152,23 @@ def scenario_rank_dies(rank, world):
     return "no error"
 
 
+def scenario_export_fails(rank, world):
+    """The fused all-gather's output buffer cannot be exported on rank 1 (as under torch's
+    expandable segments): every rank raises the same explanatory error, none waits."""
+    from my_nvfp4_gemm_b200 import capi, sharded
+    if rank == 1:
+        def export(ptr):
+            raise capi.NvFp4Error(4, "nvfp4_ipc_export")
+    else:
+        def export(ptr):
+            return b"\0" * capi.IPC_HANDLE_BYTES, 0
+    capi.ipc_export = export
+    sharded.PeerOutput(16, 32, torch.device("cpu"))
+    return "no error"
+
+
 SCENARIOS = {
+    "export_fails": scenario_export_fails,
     "gather": scenario_gather,
     "row_quantize": scenario_row_quantize,
     "unequal_widths": scenario_unequal_widths,
@@ -185,3 +201,9 @@ def test_dead_rank_surfaces_as_error_not_hang():
     res = run_ranks("rank_dies", timeout=90)
     assert res[1][0] == "err" and "injected failure" in res[1][1]
     assert res[0][0] == "err", f"rank 0 should see its collective fail, got {res[0]}"
+
+
+def test_ipc_export_failure_raises_on_every_rank():
+    res = run_ranks("export_fails")
+    for rank, (status, out) in res.items():
+        assert status == "err" and "expandable_segments" in out and "rank(s) [1]" in out, (rank, out)
