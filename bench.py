@@ -424,6 +424,14 @@ def run_ours(args):
         "clocks": clocks,
     }
 
+    # ---- the sharded workloads at this N (prefill and decode, weight sharded along N); measured
+    # right after the headline, before the host-copy and quantize sections
+    if not args.no_sharded and size == 8192:
+        summary, n_launch = sharded_summary(torch, plugins, capi, world, rank, args.steps,
+                                            args.warmup, flush, stream_h, hbm_gbs)
+        line.update(summary)
+        line["gpu_launches"] += n_launch
+
     # ---- quantize / dequantize (8192x8192 activation with 0.5% x50 outliers, seed 1)
     if not args.no_quant and size == 8192:
         g = torch.Generator(device="cuda").manual_seed(1)
@@ -583,13 +591,6 @@ def run_ours(args):
                               "consecutive steps on two streams (copies overlap across steps)"}
         line["gpu_launches"] += e2e_steps
 
-    # ---- the sharded workloads at this N (prefill and decode, weight sharded along N)
-    if not args.no_sharded and size == 8192:
-        summary, n_launch = sharded_summary(torch, plugins, capi, world, rank, args.steps,
-                                            args.warmup, flush, stream_h, hbm_gbs)
-        line.update(summary)
-        line["gpu_launches"] += n_launch
-
     # ---- CPU baseline (rank 0, N = 1 only)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_gemm(a, b, a_sf, b_sf, scale)
@@ -741,14 +742,15 @@ def sharded_summary(torch, plugins, capi, world, rank, steps, warmup, flush, str
     torch.cuda.empty_cache()
     dec = {"workload": "decode_m{16,128}_n28672_k8192", "scaling": "strong",
            "l2": "weight copies (> 3 x L2 together) in rotation, calls back to back"}
-    n_d = max(3, min(steps, 200))
+    # decode calls take ~15-30 us: a fixed 300 back-to-back calls after 30 untimed ones (~10 ms)
+    n_d, w_d = 300, 30
     for m in (16, 128):
         inp = sharded_inputs(torch, plugins, "decode", m, world, rank)
         ms = time_sharded(torch, sharded_step(torch, capi, sharded, inp, "rotate", stream_h),
-                          "rotate", n_d, warmup, flush, world)
+                          "rotate", n_d, w_d, flush, world)
         dec[f"m{m}"] = {"us_per_step": ms * 1e3, "n_per_rank": inp["n_loc"], "steps": n_d,
-                        "roofline": sharded_roofline(inp, ms, world, hbm_gbs)}
-        launches += n_d + warmup
+                        "warmup": w_d, "roofline": sharded_roofline(inp, ms, world, hbm_gbs)}
+        launches += n_d + w_d
         del inp
         torch.cuda.empty_cache()
     out["decode"] = dec
