@@ -110,6 +110,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // on the stream, when this grid was launched with programmatic stream serialization) have
 // completed and their memory operations are visible; returns at once otherwise.
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Programmatic dependent launch: this CTA no longer holds back the launch of the next kernel on
+// the stream (which still waits for this grid's completion before touching memory).
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // Streaming 16-byte global load that does not allocate in L1 (read-once data).
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
@@ -128,6 +133,11 @@ __device__ __forceinline__ uint8_t ld_nc_u8(const void* p) {
   uint16_t v;
   asm volatile("ld.global.nc.u8 %0, [%1];" : "=h"(v) : "l"(p));
   return static_cast<uint8_t>(v);
+}
+__device__ __forceinline__ void st_global_v4(void* p, uint4 v) {
+  asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
 }
 // Streaming 16-byte global store (.cs: cached evict-first, for large outputs written once).
 __device__ __forceinline__ void st_stream_v4(void* p, uint4 v) {
@@ -289,11 +299,27 @@ __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorM
       : "memory");
 }
 
+// L2 prefetch of a tile (no shared-memory write, no completion to wait for).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src,
                                              int32_t x, int32_t y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::
                    "l"(reinterpret_cast<uint64_t>(map)),
                "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+// Same, with the shared-memory source given as a shared-window address.
+__device__ __forceinline__ void tma_store_2d_s(const CUtensorMap* map, uint32_t smem_src, int32_t x,
+                                               int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::
+                   "l"(reinterpret_cast<uint64_t>(map)),
+               "r"(smem_src), "r"(x), "r"(y)
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit_group() {
