@@ -29,3 +29,15 @@ def test_two_rank_sharded_quantize_gemm_gather():
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=360)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "rank 0: ok" in r.stdout and "rank 1: ok" in r.stdout
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("M,n_loc,K", [(300, 520, 2560), (96, 1024, 512)])
+def test_fused_allgather_two_gpus_one_process(M, n_loc, K):
+    """The fused GEMM + all-gather with both ranks driven from one process (peer access instead of
+    IPC handles): every rank's output equals the single-GPU GEMM bit for bit."""
+    cmd = ["timeout", "-k", "30", "300", sys.executable, os.path.join(HERE, "fused_allgather_1proc.py"),
+           "2", str(M), str(n_loc), str(K), "2"]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=360)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "outputs bit-identical" in r.stdout
