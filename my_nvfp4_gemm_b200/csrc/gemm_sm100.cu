@@ -71,8 +71,14 @@ constexpr int kThreads = 32 * 11;
 // ~440 GB/s with 64-byte rows); 32 halves the staging memory.
 // EPI_BUFS: staging buffers per epilogue warp (a warp fills one while the TMA unit reads the
 // other).
+// KSPLIT (single-CTA form, bf16 output): the K range of a tile is split over KSPLIT CTAs of one
+// cluster, each CTA one tile and K / KSPLIT of it. Decode shapes sharded along N leave too few
+// 256-column tiles for the SMs, and each CTA's MMA chain (K / 64 block-scaled MMAs at a fixed
+// cost of ~130 cycles each when interleaved with barrier waits, whatever N) then bounds the
+// call; splitting K divides the chain. The epilogue sums the fp32 partials across the cluster
+// in a fixed order (see the split epilogue).
 template <int BN_, int STAGES_, int ACC_STAGES_, bool PAIR_, int SF_KB_, int SF_SLOTS_,
-          int EPI_COLS_ = 32, int EPI_BUFS_ = 1>
+          int EPI_COLS_ = 32, int EPI_BUFS_ = 1, int KSPLIT_ = 1>
 struct Cfg {
   static constexpr int BN = BN_;
   static constexpr int EPI_COLS = EPI_COLS_;
@@ -92,6 +98,10 @@ struct Cfg {
   static constexpr int B_ROWS = BN / CTAS;                 // B rows each CTA loads
   static_assert(BN == 256 || (!PAIR && (BN == 32 || BN == 64 || BN == 128)),
                 "BN must be 256, or 32/64/128 for the single-CTA form");
+  static constexpr int KSPLIT = KSPLIT_;
+  static_assert(KSPLIT == 1 || ((KSPLIT == 2 || KSPLIT == 4 || KSPLIT == 8) && !PAIR && SF_KB == 1 &&
+                                BN % (8 * KSPLIT) == 0),
+                "KSPLIT: 1, or 2/4/8 in the single-CTA form with one-k-block scale-factor slots");
 
   static constexpr int A_STAGE = kRowsPerCta * kBKBytes;   // 16 KiB
   static constexpr int B_STAGE = B_ROWS * kBKBytes;
@@ -110,6 +120,12 @@ struct Cfg {
   static constexpr int SMEM_BYTES = OFF_QTAB + 256 * 4;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;     // slack to align the base to 1 KiB
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget exceeded");
+  // Split epilogue: the fp32 partial tile, kRowsPerCta rows of BN + 4 floats (16-byte aligned
+  // rows whose 16-byte chunks fall in distinct bank groups for the 8 lanes of a store phase),
+  // goes in the A/B ring, idle once the tile's MMAs are done.
+  static constexpr int PART_STRIDE = BN + 4;
+  static_assert(KSPLIT == 1 || kRowsPerCta * PART_STRIDE * 4 <= STAGES * (A_STAGE + B_STAGE),
+                "split epilogue: the partial tile must fit in the A/B ring");
 
   // Tensor memory columns: accumulators, then one scale-factor slot per pipeline stage, so the
   // factors of later fills are written while the MMAs of earlier ones still read theirs. Within
@@ -185,19 +201,38 @@ __device__ __forceinline__ void write_sf_slot(uint32_t slot, uint32_t sfa_s, uin
                                               int q, int lane) {
   constexpr int kChunksB = C::BN / 32;
   constexpr int kStep = int(C::SFB_COLS_PER_STEP);
-  uint32_t vb[C::SFB_PART];
+  if constexpr (kChunksB == kStep) {
+    uint32_t vb[C::SFB_PART];
 #pragma unroll
-  for (int i = 0; i < int(C::SFB_PART); ++i) vb[i] = 0u;  // padding columns (BN < 256)
+    for (int i = 0; i < kChunksB; ++i) {
+      const uint4 w = ptx::ld_shared_v4(sf_chunk_addr<C>(sfb_s, 32 * i + lane, c));
+      vb[0 * kStep + i] = w.x;
+      vb[1 * kStep + i] = w.y;
+      vb[2 * kStep + i] = w.z;
+      vb[3 * kStep + i] = w.w;
+    }
+    ptx::tmem_st_32x32b_x32(slot, vb);
+  } else {
+    // BN < 256: only the BN/32 columns of each K-step that the MMA reads are written (the rest of
+    // the step's 8 columns is alignment padding).
+    uint32_t w[kChunksB][4];
 #pragma unroll
-  for (int i = 0; i < kChunksB; ++i) {
-    const uint4 w = ptx::ld_shared_v4(sf_chunk_addr<C>(sfb_s, 32 * i + lane, c));
-    vb[0 * kStep + i] = w.x;
-    vb[1 * kStep + i] = w.y;
-    vb[2 * kStep + i] = w.z;
-    vb[3 * kStep + i] = w.w;
+    for (int i = 0; i < kChunksB; ++i) {
+      const uint4 v = ptx::ld_shared_v4(sf_chunk_addr<C>(sfb_s, 32 * i + lane, c));
+      w[i][0] = v.x;
+      w[i][1] = v.y;
+      w[i][2] = v.z;
+      w[i][3] = v.w;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t col = slot + uint32_t(j * kStep);
+      if constexpr (kChunksB == 1) ptx::tmem_st_32x32b_x1(col, w[0][j]);
+      else if constexpr (kChunksB == 2) ptx::tmem_st_32x32b_x2(col, w[0][j], w[1][j]);
+      else ptx::tmem_st_32x32b_x4(col, w[0][j], w[1][j], w[2][j], w[3][j]);
+    }
   }
   const uint4 a = ptx::ld_shared_v4(sf_chunk_addr<C>(sfa_s, 32 * q + lane, c));
-  ptx::tmem_st_32x32b_x32(slot, vb);
   // A: quarter q's MMA reads K-step j's factors from column SFB_PART + 4j + q only; the other
   // three columns of each group belong to the other quarters' lanes and are left alone.
   const uint32_t sfa = slot + C::SFB_PART + uint32_t(q);
@@ -247,7 +282,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
             const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
             const __grid_constant__ DstMaps<NDST> dst, const Params p) {
   constexpr bool kPair = C::PAIR;
+  constexpr int kSplit = C::KSPLIT;
   static_assert(MODE == kEpiBf16 || C::BN == 256, "epilogue variants use 256-column tiles");
+  static_assert(kSplit == 1 || (MODE == kEpiBf16 && NDST == 1), "split K: plain bf16 output");
   constexpr int kGroup = C::CTAS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -275,8 +312,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   const int lane = threadIdx.x & 31;
   const uint32_t rank = kPair ? ptx::cluster_ctarank() : 0u;
   const int num_tiles = p.m_blocks * p.n_blocks;
-  const int first_tile = kPair ? int(blockIdx.x >> 1) : int(blockIdx.x);
-  const int tile_step = kPair ? int(gridDim.x >> 1) : int(gridDim.x);
+  // Split K: cluster c works on tile c (one tile per cluster), its CTA s on k-blocks
+  // [s * k_stages / KSPLIT, (s + 1) * k_stages / KSPLIT).
+  const int split = kSplit > 1 ? int(ptx::cluster_ctarank()) : 0;
+  const int first_tile = kPair ? int(blockIdx.x >> 1) : int(blockIdx.x) / kSplit;
+  const int tile_step = kPair ? int(gridDim.x >> 1) : int(gridDim.x) / kSplit;
+  const int kb_count = p.k_stages / kSplit;
+  const int kb_lo = split * kb_count;
+  const int kb_hi = kb_lo + kb_count;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
@@ -307,7 +350,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     ptx::tmem_relinquish_g<kGroup>();
   }
   ptx::tc_fence_before_sync();
-  if constexpr (kPair) ptx::cluster_sync(); else __syncthreads();
+  if constexpr (kPair || kSplit > 1) ptx::cluster_sync(); else __syncthreads();
   ptx::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -325,9 +368,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       int mb, nb;
       tile_coords(first_tile, p, mb, nb);
       const int n_cta = nb * C::BN + int(rank) * C::B_ROWS;
-      for (int kb = 0; kb < C::STAGES && kb < p.k_stages; ++kb)
+      for (int kb = kb_lo; kb < kb_lo + C::STAGES && kb < kb_hi; ++kb)
         ptx::tma_prefetch_2d(&tm_b, kb * kBKBytes, n_cta);
-      ptx::tma_prefetch_2d(&tm_sfb, 0, nb * C::BN);
+      ptx::tma_prefetch_2d(&tm_sfb, kb_lo * kSfBytesPerRow, nb * C::BN);
     }
     ptx::griddep_wait();
   }
@@ -342,7 +385,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         tile_coords(tile, p, mb, nb);
         const int m_cta = mb * C::TILE_M + int(rank) * kRowsPerCta;
         const int n_cta = nb * C::BN + int(rank) * C::B_ROWS;
-        for (int kb = 0; kb < p.k_stages; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!ptx::mbar_wait<kPair>(&empty_bar[stage], phase ^ 1, abort_flag, p.timeout_ns))
             goto producer_done;
           if (rank == 0) ptx::mbar_arrive_expect_tx(&full_bar[stage], p.ab_tx);
@@ -380,7 +423,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         tile_coords(tile, p, mb, nb);
         const int row_a = mb * C::TILE_M + int(rank) * kRowsPerCta;
         const int row_b = nb * C::BN;
-        for (int kb = 0; kb < p.k_stages; kb += C::SF_KB) {
+        for (int kb = kb_lo; kb < kb_hi; kb += C::SF_KB) {
           if (!ptx::mbar_wait<kPair>(&sempty_bar[slot], phase ^ 1, abort_flag, p.timeout_ns))
             goto sf_producer_done;
           ptx::mbar_arrive_expect_tx(&sfull_bar[slot], p.sf_tx);
@@ -424,7 +467,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
           goto mma_done;
         ptx::tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * C::BN);
-        for (int kb = 0; kb < p.k_stages; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!ptx::mbar_wait<kPair>(&full_bar[stage], phase, abort_flag, p.timeout_ns)) goto mma_done;
           ptx::tc_fence_after_sync();
           const uint64_t a_desc = a_desc0 + uint32_t(stage) * kADescStep;
@@ -433,14 +476,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
           const uint32_t t_sfa = t_sfb + C::SFB_PART;
           // K-step j starts 32 bytes (2 descriptor units) further along the swizzled rows.
           if constexpr (kPair) {
-            ptx::tc_mma_mxf4nvf4_pair(d_tmem, a_desc, b_desc, idesc, t_sfa, t_sfb, kb != 0 ? 1u : 0u);
+            ptx::tc_mma_mxf4nvf4_pair(d_tmem, a_desc, b_desc, idesc, t_sfa, t_sfb, kb != kb_lo ? 1u : 0u);
 #pragma unroll
             for (int j = 1; j < kKSteps; ++j)
               ptx::tc_mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * j, b_desc + 2 * j, idesc, t_sfa + 4 * j,
                                         t_sfb + j * C::SFB_COLS_PER_STEP, 1u);
             ptx::tc_commit_pair(&empty_bar[stage], 0x3);  // stage free in both CTAs
           } else {
-            ptx::tc_mma_mxf4nvf4(d_tmem, a_desc, b_desc, idesc, t_sfa, t_sfb, kb != 0 ? 1u : 0u);
+            ptx::tc_mma_mxf4nvf4(d_tmem, a_desc, b_desc, idesc, t_sfa, t_sfb, kb != kb_lo ? 1u : 0u);
 #pragma unroll
             for (int j = 1; j < kKSteps; ++j)
               ptx::tc_mma_mxf4nvf4(d_tmem, a_desc + 2 * j, b_desc + 2 * j, idesc, t_sfa + 4 * j,
@@ -477,7 +520,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     int slot = 0;
     uint32_t slot_phase = 0;
     for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
-      for (int kb = 0; kb < p.k_stages; ++kb) {
+      for (int kb = kb_lo; kb < kb_hi; ++kb) {
         const int c = kb % C::SF_KB;
         bool ok = true;
         if (c == 0) ok = ptx::mbar_wait<kPair>(&sfull_bar[slot], slot_phase, abort_flag, p.timeout_ns);
@@ -494,7 +537,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
           if constexpr (kPair) ptx::mbar_arrive_cta(&full_bar[stage], 0);
           else ptx::mbar_arrive(&full_bar[stage]);
         }
-        if (c == C::SF_KB - 1 || kb == p.k_stages - 1) {
+        if (c == C::SF_KB - 1 || kb == kb_hi - 1) {
           if (lane == 0) ptx::mbar_arrive(&sempty_bar[slot]);
           if (++slot == C::SF_SLOTS) { slot = 0; slot_phase ^= 1; }
         }
@@ -506,7 +549,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
     // ------------------------------------------------------------------ epilogue
     const int ew = warp - kFirstEpiWarp;  // == warp % 4: TMEM lanes 32*ew .. 32*ew+31
     // Single-CTA bf16 form (decode shapes, usually one tile per CTA): see the store loop.
-    constexpr bool kRingStage = !kPair && NDST == 1 && MODE == kEpiBf16;
+    constexpr bool kRingStage = !kPair && kSplit == 1 && NDST == 1 && MODE == kEpiBf16;
     static_assert(!kRingStage || kNumEpiWarps * 64 * C::BN <= C::STAGES * (C::A_STAGE + C::B_STAGE),
                   "the A/B ring must hold every epilogue warp's boxes of one tile");
     const float scale = p.scale_ptr ? __ldg(p.scale_ptr) : p.scale_val;
@@ -525,6 +568,85 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         tab[i] = bq::os_of_scale_byte(uint32_t(i), rcp_s_out);
       asm volatile("bar.sync 1, %0;" ::"n"(kNumEpiWarps * 32) : "memory");  // epilogue warps only
     }
+    if constexpr (kSplit > 1) {
+      // Split K (one tile per cluster). Step 1: this CTA's fp32 partial rows that lie inside D go
+      // to the idle A/B ring (the tile's MMAs, which tfull waited for, consumed every fill).
+      // Step 2: cluster barrier, which every thread of the cluster passes exactly once before
+      // the final one, on the abort path too. Step 3: CTA s owns columns [s, s + 1) * BN /
+      // KSPLIT of the tile: the KSPLIT partials summed in split order (fp32 adds, round to
+      // nearest), times 1/scale, to bf16, 4 columns per task, read from each CTA's shared
+      // memory, which stays valid until the final cluster barrier.
+      int mb, nb;
+      tile_coords(first_tile, p, mb, nb);
+      const int m_cta = mb * C::TILE_M;
+      const int n0 = nb * C::BN;
+      const uint32_t part_s = ptx::smem_u32(smem + C::OFF_A);
+      const bool ok = __all_sync(0xFFFFFFFFu, first_tile < num_tiles &&
+                                                  ptx::mbar_wait<false>(&tfull_bar[0], 0, abort_flag,
+                                                                        p.timeout_ns));
+      if (ok && m_cta + ew * 32 < p.m) {
+        ptx::tc_fence_after_sync();
+        const uint32_t t_row = tmem_base + (uint32_t(ew * 32) << 16);
+        const int row = ew * 32 + lane;
+#pragma unroll
+        for (int g = 0; g < C::BN / 64; ++g) {  // 64 columns per tcgen05.wait::ld
+          uint32_t v[64];
+          ptx::tmem_ld_32x32b_x32(t_row + g * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
+          ptx::tmem_ld_32x32b_x32(t_row + g * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+          ptx::tmem_wait_ld();
+          if (m_cta + row < p.m) {
+            const uint32_t dst_s = part_s + uint32_t((row * C::PART_STRIDE + g * 64) * 4);
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+              ptx::st_shared_v4(dst_s + 16 * k,
+                                make_uint4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+          }
+        }
+      }
+      ptx::cluster_sync();
+      // Every load and MMA of the cluster is over: the next kernel on the stream may launch (it
+      // still waits for this grid's completion before reading memory).
+      if (ew == 0 && lane == 0) ptx::griddep_launch_dependents();
+      if (ok && !*abort_flag) {
+        constexpr int kCols = C::BN / kSplit;
+        constexpr int kQuads = kCols / 4;
+        const int rows = min(kRowsPerCta, p.m - m_cta);
+        const int tasks = rows * kQuads;
+        constexpr int kStride = kNumEpiWarps * 32;
+        // Two tasks per iteration, all 2 * KSPLIT cluster loads issued before the first add.
+        for (int task = ew * 32 + lane; task < tasks; task += 2 * kStride) {
+          uint4 part[2][kSplit];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int tk = min(task + h * kStride, tasks - 1);
+            const uint32_t src = part_s + uint32_t(((tk / kQuads) * C::PART_STRIDE +
+                                                    split * kCols + (tk % kQuads) * 4) * 4);
+#pragma unroll
+            for (int t = 0; t < kSplit; ++t)
+              part[h][t] = ptx::ld_dsmem_v4(ptx::map_addr_to_cta(src, uint32_t(t)));
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int tk = task + h * kStride;
+            const int col = split * kCols + (tk % kQuads) * 4;
+            // N % 8 == 0: a quad lies wholly inside or outside D
+            if (tk >= tasks || n0 + col >= p.n) continue;
+            float s0 = __uint_as_float(part[h][0].x), s1 = __uint_as_float(part[h][0].y);
+            float s2 = __uint_as_float(part[h][0].z), s3 = __uint_as_float(part[h][0].w);
+#pragma unroll
+            for (int t = 1; t < kSplit; ++t) {
+              s0 = __fadd_rn(s0, __uint_as_float(part[h][t].x));
+              s1 = __fadd_rn(s1, __uint_as_float(part[h][t].y));
+              s2 = __fadd_rn(s2, __uint_as_float(part[h][t].z));
+              s3 = __fadd_rn(s3, __uint_as_float(part[h][t].w));
+            }
+            *reinterpret_cast<uint2*>(p.d + int64_t(m_cta + tk / kQuads) * p.ldd + n0 + col) =
+                make_uint2(ptx::scaled_f32x2_to_bf16x2(__float_as_uint(s0), __float_as_uint(s1), alpha2),
+                           ptx::scaled_f32x2_to_bf16x2(__float_as_uint(s2), __float_as_uint(s3), alpha2));
+          }
+        }
+      }
+    } else {
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
@@ -700,10 +822,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
         ptx::bulk_wait_group_read<0>();
       }
     }
+    }  // not split K
   }
 
+  if constexpr (kSplit > 1) {
+    // Split K: the epilogue warps pass the cluster's partials barrier inside their role; every
+    // other warp passes it here, so that each thread of the cluster arrives exactly once.
+    if (!(warp >= kFirstEpiWarp && warp < kFirstEpiWarp + kNumEpiWarps)) ptx::cluster_sync();
+  }
   ptx::tc_fence_before_sync();
-  if constexpr (kPair) ptx::cluster_sync(); else __syncthreads();
+  // Pairs and split-K clusters: no CTA exits (releasing its shared memory) while a peer may
+  // still read it.
+  if constexpr (kPair || kSplit > 1) ptx::cluster_sync(); else __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) atomicCAS(&g_nvfp4_device_status, 0, NVFP4_ERR_DEVICE_TIMEOUT);
   if (warp == kMmaWarp) {
     __syncwarp();
@@ -828,6 +958,11 @@ using CfgPair = Cfg<256, 5, 1, true, 4, 2, 64, 1>;
 using CfgSingle128 = Cfg<128, 6, 1, false, 1, 4>;
 using CfgSingle64 = Cfg<64, 8, 1, false, 1, 4>;
 using CfgSingle32 = Cfg<32, 10, 1, false, 1, 4>;
+// 128 x 256 tiles with K split over a cluster of 4 or 8 CTAs (decode shapes whose 256-column
+// tiles fill less than half the SMs, K a multiple of KSPLIT k-blocks). A split over 2 CTAs was
+// slower than the 128-column tiles below at the widths that would take it.
+using CfgSplit4 = Cfg<256, 4, 1, false, 1, 4, 32, 1, 4>;
+using CfgSplit8 = Cfg<256, 4, 1, false, 1, 4, 32, 1, 8>;
 
 // D of this launch: `count` destinations, each [M, N] with its own base and row pitch.
 struct DstDesc {
@@ -852,6 +987,7 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
   const int units = resident_units<C, NDST, MODE>(dev);
   if (units <= 0) return units == 0 ? NVFP4_ERR_NO_DEVICE : -units;
   if (dd.count < 1 || dd.count > NDST) return NVFP4_ERR_INVALID_VALUE;
+  if ((K / kBK) % C::KSPLIT != 0) return NVFP4_ERR_INVALID_VALUE;
 
   CUtensorMap tm_a, tm_b, tm_sfa, tm_sfb;
   DstMaps<NDST> dst;
@@ -906,14 +1042,16 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
   p.d = static_cast<uint16_t*>(dd.base[0]);
   p.ldd = int64_t(dd.row_bytes / 2);
   const int64_t tiles = int64_t(p.m_blocks) * p.n_blocks;
-  if (tiles > 0x7FFFFFFF / 2) return NVFP4_ERR_TOO_LARGE;
-  const int grid_units = int(tiles < units ? tiles : units);
+  if (tiles > 0x7FFFFFFF / 16) return NVFP4_ERR_TOO_LARGE;
+  // Split K: one cluster of KSPLIT CTAs per tile (clusters beyond what fits at once run as
+  // earlier ones finish; each cluster only waits on its own CTAs). Otherwise a persistent grid.
+  const int grid_units = C::KSPLIT > 1 ? int(tiles) : int(tiles < units ? tiles : units);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   int na = 0;
-  if constexpr (C::PAIR) {
+  if constexpr (C::PAIR || C::KSPLIT > 1) {
     attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = 2;
+    attr[na].val.clusterDim.x = C::PAIR ? 2 : C::KSPLIT;
     attr[na].val.clusterDim.y = 1;
     attr[na].val.clusterDim.z = 1;
     ++na;
@@ -925,7 +1063,7 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
   }
-  cfg.gridDim = dim3(C::CTAS * grid_units);
+  cfg.gridDim = dim3(C::CTAS * C::KSPLIT * grid_units);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::SMEM_ALLOC;
   cfg.stream = stream;
@@ -962,6 +1100,13 @@ int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const 
   const int sms = current_device_sm_count(nullptr);
   const auto tiles = [N](int64_t bn) { return (N + bn - 1) / bn; };
   if (sms > 0 && 2 * tiles(256) <= sms) {
+    // Split K over the widest cluster that still fits every tile's cluster on the SMs at once.
+    const int64_t kblocks = K / kBK;
+    const auto split_fits = [&](int64_t s) { return tiles(256) * s <= sms && kblocks % s == 0; };
+    if (split_fits(8))
+      return launch<CfgSplit8, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+    if (split_fits(4))
+      return launch<CfgSplit4, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
     if (2 * tiles(128) > sms)
       return launch<CfgSingle128, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
     if (2 * tiles(64) > sms)

@@ -242,6 +242,16 @@ __device__ __forceinline__ void mbar_arrive_cta(uint64_t* local, uint32_t rank) 
                : "memory");
 }
 // All threads of all CTAs in the cluster.
+// Arrive on the barrier at `local`'s offset in cluster CTA `rank`, releasing this thread's prior
+// writes (and those it has synchronised with) at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster_release(uint64_t* local, uint32_t rank) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   map_to_cta(local, rank))
+               : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() {
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
@@ -487,6 +497,16 @@ __device__ __forceinline__ void tmem_wait_ld() {
 // Each thread of the warp writes N consecutive 32-bit columns of its own TMEM lane.
 __device__ __forceinline__ void tmem_st_32x32b_x1(uint32_t taddr, uint32_t v) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void tmem_st_32x32b_x2(uint32_t taddr, uint32_t v0, uint32_t v1) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(v0), "r"(v1)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, uint32_t v0, uint32_t v1,
+                                                  uint32_t v2, uint32_t v3) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
+               "r"(v0), "r"(v1), "r"(v2), "r"(v3)
+               : "memory");
 }
 __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
