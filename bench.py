@@ -89,6 +89,9 @@ def parse_args():
     ap.add_argument("--swiglu", action="store_true",
                     help="prefill: the weight is gate+up (2 x 28672 rows); SwiGLU in the GEMM "
                          "epilogue, output [M, 28672]")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="prefill/decode on one GPU: time rank 0's column shard of a P-way split "
+                         "alone (the per-rank workload of a P-GPU run; profiling)")
     ap.add_argument("--fused-gather", action="store_true",
                     help="with --gather: the all-gather fused into the GEMM epilogue (stores into "
                          "every rank's output over NVLink) instead of NCCL")
@@ -768,7 +771,11 @@ def run_sharded_workload(args):
     swiglu = bool(args.swiglu and args.workload == "prefill")
     if swiglu and args.gather:
         raise SystemExit("--swiglu and --gather are separate measurements")
-    inp = sharded_inputs(torch, plugins, args.workload, args.m, world, rank, swiglu=swiglu)
+    shard_of = args.shard_of
+    if shard_of > 1 and (world > 1 or args.gather):
+        raise SystemExit("--shard-of times one rank's shard alone on one GPU (no gather)")
+    inp = sharded_inputs(torch, plugins, args.workload, args.m, max(world, shard_of), rank,
+                         swiglu=swiglu)
     M, N, K, n_loc = inp["M"], inp["N"], inp["K"], inp["n_loc"]
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     stream_h = torch.cuda.current_stream().cuda_stream
@@ -787,7 +794,7 @@ def run_sharded_workload(args):
     sampler = ClockSampler(gpu_uuid(torch, torch.cuda.current_device()))
     with sampler:
         ms = time_sharded(torch, step, mode, args.steps, args.warmup, flush, world)
-    flops = 2.0 * M * N * K
+    flops = 2.0 * M * (n_loc if shard_of > 1 else N) * K
     rl = sharded_roofline(inp, ms, world, hbm_gbs, gather=mode in ("fused", "nccl"))
     decode = M <= 128
     line = {
@@ -795,8 +802,9 @@ def run_sharded_workload(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "e2m1/ue4m3->f32", "data": "synthetic",
-        "config": {"workload": inp["name"], "M": M, "N": N, "K": K, "n_per_rank": n_loc,
-                   "parallelism": f"column-parallel N x{world}",
+        "config": {"workload": inp["name"] + (f"_shard0of{shard_of}" if shard_of > 1 else ""), "M": M, "N": N, "K": K, "n_per_rank": n_loc,
+                   "parallelism": (f"rank 0's shard of column-parallel N x{shard_of}, alone on one "
+                                   "GPU" if shard_of > 1 else f"column-parallel N x{world}"),
                    "all_gather_in_timing": mode in ("fused", "nccl"),
                    "epilogue": ("SwiGLU (gate+up interleaved in 128-row groups), output "
                                 f"[M, {N // 2}]" if swiglu else "bf16 D"),
@@ -811,7 +819,8 @@ def run_sharded_workload(args):
                           "peak": hbm_gbs if decode else NOMINAL_FP4_TFLOPS,
                           "unit": "GB/s" if decode else "TFLOP/s",
                           "frac": rl["frac_hbm_per_rank"] if decode else rl["frac_fp4_peak_per_rank"],
-                          "traffic": (profiled_traffic(f"gemm_decode_m{M}")
+                          "traffic": (profiled_traffic(f"gemm_decode_m{M}" + (
+                                          f"_shard0of{shard_of}" if shard_of > 1 else ""))
                                       if args.workload == "decode" and world == 1 else None),
                           "peak_source": f"{peak_src} HBM {hbm_gbs} GB/s; FP4 dense 9.0 PFLOP/s "
                                          "(nominal)"}, **rl),
