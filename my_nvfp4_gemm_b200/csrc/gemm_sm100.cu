@@ -958,11 +958,12 @@ using CfgPair = Cfg<256, 5, 1, true, 4, 2, 64, 1>;
 using CfgSingle128 = Cfg<128, 6, 1, false, 1, 4>;
 using CfgSingle64 = Cfg<64, 8, 1, false, 1, 4>;
 using CfgSingle32 = Cfg<32, 10, 1, false, 1, 4>;
-// 128 x 256 tiles with K split over a cluster of 4 or 8 CTAs (decode shapes whose 256-column
-// tiles fill less than half the SMs, K a multiple of KSPLIT k-blocks). A split over 2 CTAs was
-// slower than the 128-column tiles below at the widths that would take it.
+// K split over a cluster of KSPLIT CTAs (decode shapes whose 256-column tiles fill less than
+// half the SMs, K a multiple of KSPLIT k-blocks): 128 x 128 tiles over 4 or 2 CTAs, 128 x 256
+// tiles over 4. The narrower tile halves the partials each CTA exchanges in the cluster sum.
+using CfgSplit4N128 = Cfg<128, 6, 1, false, 1, 4, 32, 1, 4>;
+using CfgSplit2N128 = Cfg<128, 6, 1, false, 1, 4, 32, 1, 2>;
 using CfgSplit4 = Cfg<256, 4, 1, false, 1, 4, 32, 1, 4>;
-using CfgSplit8 = Cfg<256, 4, 1, false, 1, 4, 32, 1, 8>;
 
 // D of this launch: `count` destinations, each [M, N] with its own base and row pitch.
 struct DstDesc {
@@ -1100,12 +1101,16 @@ int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const 
   const int sms = current_device_sm_count(nullptr);
   const auto tiles = [N](int64_t bn) { return (N + bn - 1) / bn; };
   if (sms > 0 && 2 * tiles(256) <= sms) {
-    // Split K over the widest cluster that still fits every tile's cluster on the SMs at once.
+    // Split K when every tile's cluster fits on the SMs at once (measured on 28672 / 8 and / 4
+    // column shards of a 28672 x 8192 weight): 128-column tiles over 4 CTAs where they fit;
+    // else, above 32 rows, 128-column tiles over 2; else 256-column tiles over 4.
     const int64_t kblocks = K / kBK;
-    const auto split_fits = [&](int64_t s) { return tiles(256) * s <= sms && kblocks % s == 0; };
-    if (split_fits(8))
-      return launch<CfgSplit8, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
-    if (split_fits(4))
+    const auto fits = [&](int64_t bn, int64_t s) { return tiles(bn) * s <= sms && kblocks % s == 0; };
+    if (fits(128, 4))
+      return launch<CfgSplit4N128, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+    if (M > 32 && fits(128, 2))
+      return launch<CfgSplit2N128, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+    if (fits(256, 4))
       return launch<CfgSplit4, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
     if (2 * tiles(128) > sms)
       return launch<CfgSingle128, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
