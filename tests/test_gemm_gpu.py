@@ -267,6 +267,30 @@ def test_gemm_skinny_decode_shape(plugins, oracle, M):
     assert_gemm_close(d.view(torch.int16).cpu().numpy().view(np.uint16), ref, f"M={M} skinny")
 
 
+# Decode shapes whose 256-column tiles fill less than half the SMs split K over a cluster:
+# 128-column tiles over 4 CTAs where they fit, else (M > 32) 128-column tiles over 2, else
+# 256-column tiles over 4. Each form, with M = 1, M just above 32, one k-block per CTA and
+# ragged N (a last tile of 104 and of 8 columns).
+SPLIT_SHAPES = [
+    (1, 3584, 2048),      # 128-column tiles over 4 (28 tiles, 2 k-blocks per CTA)
+    (33, 3584, 1024),     # same form, M just above 32, one k-block per CTA
+    (7, 1000, 4096),      # same form, last tile 104 columns wide
+    (100, 7168, 2048),    # 128-column tiles over 2 (56 tiles), M > 32
+    (24, 7168, 2048),     # 256-column tiles over 4 (28 tiles), M <= 32
+    (128, 7176, 1024),    # 128-column tiles over 2, last tile 8 columns wide
+]
+
+
+@pytest.mark.parametrize("M,N,K", SPLIT_SHAPES)
+def test_gemm_split_k_decode_shapes(oracle, M, N, K):
+    rng = np.random.default_rng(M * 7 + N + K)
+    A, B, Asf, Bsf = random_operands(rng, M, N, K)
+    ref = oracle.gemm_f32(A, B, Asf, Bsf, 1.5)
+    assert_gemm_close(capi_gemm(A, B, Asf, Bsf, 1.5), ref, f"split {M}x{N}x{K}")
+    # repeated calls give the same bits (the cluster sum runs in a fixed order)
+    assert np.array_equal(capi_gemm(A, B, Asf, Bsf, 1.5), capi_gemm(A, B, Asf, Bsf, 1.5))
+
+
 @pytest.mark.parametrize("M,N,K", [(5, 520, 1024), (16, 28672, 2048), (100, 1024, 512),
                                    (130, 512, 512)])
 def test_gemm_leaves_memory_past_row_m_untouched(M, N, K):
