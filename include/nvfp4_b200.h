@@ -132,6 +132,17 @@ int nvfp4_gemm_host_scale(const void* A, const void* B, const void* A_sf, const 
                           cudaStream_t stream);
 
 /*
+ * The kernel form nvfp4_gemm runs for an M x N x K problem on a device with `sms` SMs (0: the
+ * current device): output tile rows (256 for the CTA-pair form, else 128), tile columns (256,
+ * 128, 64 or 32) and the number of CTAs K is split over (1, 2 or 4; decode shapes whose
+ * 256-column tiles fill less than half the SMs). No reference counterpart: for tests of the
+ * dispatch rules and for callers sizing column shards. Touches no device when sms > 0. Returns
+ * the same shape errors as nvfp4_gemm; K must be > 0.
+ */
+int nvfp4_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* tile_m, int* tile_n,
+                    int* k_split);
+
+/*
  * GEMM whose output is quantized to NVFP4 in the epilogue, for a layer whose consumer takes
  * NVFP4 input. No reference counterpart: it replaces nvfp4_gemm followed by nvfp4_quantize of
  * its bf16 output and produces exactly those bytes, q_out = packed E2M1 [M, N/2] and

@@ -41,6 +41,8 @@ SIGNATURES = {
     "nvfp4_dequantize_host_scale": ([_P, _F32, _P, _I64, _P, _P], _INT),
     "nvfp4_gemm": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P], _INT),
     "nvfp4_gemm_host_scale": ([_P, _P, _P, _P, _F32, _P, _I64, _I64, _I64, _P], _INT),
+    "nvfp4_gemm_plan": ([_I64, _I64, _I64, _INT, ctypes.POINTER(_INT), ctypes.POINTER(_INT),
+                         ctypes.POINTER(_INT)], _INT),
     "nvfp4_gemm_quantized": ([_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P], _INT),
     "nvfp4_gemm_swiglu": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P], _INT),
     "nvfp4_gemm_allgather": ([_P, _P, _P, _P, _P, ctypes.POINTER(_P), _INT, _INT, _I64, _I64, _I64, _P], _INT),
@@ -129,6 +131,15 @@ def gemm(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, d_ptr, m, n, k, stream=0) ->
 
 def gemm_host_scale(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale, d_ptr, m, n, k, stream=0) -> int:
     return lib().nvfp4_gemm_host_scale(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale, d_ptr, m, n, k, stream)
+
+
+def gemm_plan(m, n, k, sms=0) -> tuple[int, int, int]:
+    """(tile rows, tile columns, K split) of the kernel form nvfp4_gemm runs for M x N x K on a
+    device with `sms` SMs (0: the current device). Raises on an invalid shape."""
+    tm, tn, ks = _INT(0), _INT(0), _INT(0)
+    check(lib().nvfp4_gemm_plan(m, n, k, sms, ctypes.byref(tm), ctypes.byref(tn), ctypes.byref(ks)),
+          "nvfp4_gemm_plan")
+    return tm.value, tn.value, ks.value
 
 
 def gemm_quantized(a_ptr, b_ptr, asf_ptr, bsf_ptr, scale_ptr, out_scale_ptr, q_ptr, sf_ptr, m, n,

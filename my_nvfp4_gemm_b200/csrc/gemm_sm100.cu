@@ -1074,11 +1074,39 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
                                              tm_sfb, dst, p));
 }
 
-int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const float* scale_ptr,
-        float scale_val, void* D, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+// The kernel form of a plain bf16 GEMM, M x N x K (K > 0, a multiple of 256) on `sms` SMs.
+enum class Plan { kPair, kSingle, kSingle128, kSingle64, kSingle32, kSplit4N128, kSplit2N128, kSplit4 };
+
+Plan select_plan(int64_t M, int64_t N, int64_t K, int sms) {
+  // A CTA pair covers 256 rows; for M <= 128 a single CTA per tile wastes no tensor work.
+  if (M > kRowsPerCta) return Plan::kPair;
+  const auto tiles = [N](int64_t bn) { return (N + bn - 1) / bn; };
+  if (sms <= 0 || 2 * tiles(256) > sms) return Plan::kSingle;
+  // 256-column tiles give less than half the SMs a tile. Split K when every tile's cluster fits
+  // on the SMs at once (measured on 28672 / 8 and / 4 column shards of a 28672 x 8192 weight):
+  // 128-column tiles over 4 CTAs where they fit; else, above 32 rows, 128-column tiles over 2;
+  // else 256-column tiles over 4. Otherwise the widest single-CTA tile that still gives at least
+  // half the SMs a tile.
+  const int64_t kblocks = K / kBK;
+  const auto fits = [&](int64_t bn, int64_t s) { return tiles(bn) * s <= sms && kblocks % s == 0; };
+  if (fits(128, 4)) return Plan::kSplit4N128;
+  if (M > 32 && fits(128, 2)) return Plan::kSplit2N128;
+  if (fits(256, 4)) return Plan::kSplit4;
+  if (2 * tiles(128) > sms) return Plan::kSingle128;
+  if (2 * tiles(64) > sms) return Plan::kSingle64;
+  return Plan::kSingle32;
+}
+
+int check_shape(int64_t M, int64_t N, int64_t K) {
   if (M < 0 || N < 0 || K < 0) return NVFP4_ERR_INVALID_VALUE;
   if (K % kBK != 0 || N % 8 != 0) return NVFP4_ERR_UNSUPPORTED_SHAPE;
   if (M > 0x7FFFFFFF || N > 0x7FFFFFFF || K > 0x7FFFFFFF) return NVFP4_ERR_TOO_LARGE;
+  return NVFP4_OK;
+}
+
+int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const float* scale_ptr,
+        float scale_val, void* D, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  if (const int st = check_shape(M, N, K); st != NVFP4_OK) return st;
   if (M == 0 || N == 0) return NVFP4_OK;
   if (!D) return NVFP4_ERR_INVALID_VALUE;
   if (!aligned_to(D, 16)) return NVFP4_ERR_MISALIGNED;
@@ -1094,31 +1122,20 @@ int run(const void* A, const void* B, const void* A_sf, const void* B_sf, const 
   dd.base[0] = D;
   dd.row_bytes = uint64_t(N) * 2;
   dd.count = 1;
-  // A CTA pair covers 256 rows; for M <= 128 a single CTA per tile wastes no tensor work.
-  if (M > kRowsPerCta)
-    return launch<CfgPair, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
-  // The widest single-CTA tile that still gives at least half the SMs a tile.
-  const int sms = current_device_sm_count(nullptr);
-  const auto tiles = [N](int64_t bn) { return (N + bn - 1) / bn; };
-  if (sms > 0 && 2 * tiles(256) <= sms) {
-    // Split K when every tile's cluster fits on the SMs at once (measured on 28672 / 8 and / 4
-    // column shards of a 28672 x 8192 weight): 128-column tiles over 4 CTAs where they fit;
-    // else, above 32 rows, 128-column tiles over 2; else 256-column tiles over 4.
-    const int64_t kblocks = K / kBK;
-    const auto fits = [&](int64_t bn, int64_t s) { return tiles(bn) * s <= sms && kblocks % s == 0; };
-    if (fits(128, 4))
-      return launch<CfgSplit4N128, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
-    if (M > 32 && fits(128, 2))
-      return launch<CfgSplit2N128, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
-    if (fits(256, 4))
-      return launch<CfgSplit4, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
-    if (2 * tiles(128) > sms)
-      return launch<CfgSingle128, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
-    if (2 * tiles(64) > sms)
-      return launch<CfgSingle64, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
-    return launch<CfgSingle32, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+  const int sms = M > kRowsPerCta ? 0 : current_device_sm_count(nullptr);
+#define NVFP4_LAUNCH(CFG) launch<CFG, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream)
+  switch (select_plan(M, N, K, sms)) {
+    case Plan::kPair: return NVFP4_LAUNCH(CfgPair);
+    case Plan::kSplit4N128: return NVFP4_LAUNCH(CfgSplit4N128);
+    case Plan::kSplit2N128: return NVFP4_LAUNCH(CfgSplit2N128);
+    case Plan::kSplit4: return NVFP4_LAUNCH(CfgSplit4);
+    case Plan::kSingle128: return NVFP4_LAUNCH(CfgSingle128);
+    case Plan::kSingle64: return NVFP4_LAUNCH(CfgSingle64);
+    case Plan::kSingle32: return NVFP4_LAUNCH(CfgSingle32);
+    case Plan::kSingle: break;
   }
-  return launch<CfgSingle, 1>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N, K, stream);
+  return NVFP4_LAUNCH(CfgSingle);
+#undef NVFP4_LAUNCH
 }
 
 // Column-parallel GEMM with the all-gather fused into the epilogue. Every rank holds the same
@@ -1247,6 +1264,32 @@ int nvfp4_gemm_host_scale(const void* A, const void* B, const void* A_sf, const 
                           float scale, void* D, int64_t M, int64_t N, int64_t K,
                           cudaStream_t stream) {
   return nvfp4::gemm::run(A, B, A_sf, B_sf, nullptr, scale, D, M, N, K, stream);
+}
+
+int nvfp4_gemm_plan(int64_t M, int64_t N, int64_t K, int sms, int* tile_m, int* tile_n,
+                    int* k_split) {
+  using nvfp4::gemm::Plan;
+  if (!tile_m || !tile_n || !k_split || K == 0) return NVFP4_ERR_INVALID_VALUE;
+  if (const int st = nvfp4::gemm::check_shape(M, N, K); st != NVFP4_OK) return st;
+  if (sms <= 0) {
+    sms = nvfp4::current_device_sm_count(nullptr);
+    if (sms <= 0) return NVFP4_ERR_NO_DEVICE;
+  }
+  int tm = 128, tn = 256, ks = 1;
+  switch (nvfp4::gemm::select_plan(M, N, K, sms)) {
+    case Plan::kPair: tm = 256; break;
+    case Plan::kSingle: break;
+    case Plan::kSingle128: tn = 128; break;
+    case Plan::kSingle64: tn = 64; break;
+    case Plan::kSingle32: tn = 32; break;
+    case Plan::kSplit4N128: tn = 128; ks = 4; break;
+    case Plan::kSplit2N128: tn = 128; ks = 2; break;
+    case Plan::kSplit4: ks = 4; break;
+  }
+  *tile_m = tm;
+  *tile_n = tn;
+  *k_split = ks;
+  return NVFP4_OK;
 }
 
 int nvfp4_gemm_quantized(const void* A, const void* B, const void* A_sf, const void* B_sf,
