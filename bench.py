@@ -721,9 +721,29 @@ def sharded_roofline(inp, ms, world, hbm_gbs, gather=False):
 
 
 def sharded_summary(torch, plugins, capi, world, rank, steps, warmup, flush, stream_h, hbm_gbs):
-    """The `prefill` and `decode` keys of the square line: the sharded workloads at this N."""
+    """The `prefill` and `decode` keys of the square line: the sharded workloads at this N.
+    Decode runs first, after a short pause: right after seconds of power-capped GEMM (the
+    headline, and on one GPU the 15-PFLOP prefill steps) the clocks recover over a few tens of
+    milliseconds, and the ~10 ms decode rotation measured in that window ran ~20 % slow."""
+    import time
     from my_nvfp4_gemm_b200 import sharded
     out, launches = {}, 0
+    torch.cuda.synchronize()
+    time.sleep(0.25)
+    dec = {"workload": "decode_m{16,128}_n28672_k8192", "scaling": "strong",
+           "l2": "weight copies (> 3 x L2 together) in rotation, calls back to back"}
+    # decode calls take ~8-30 us: a fixed 300 back-to-back calls after 30 untimed ones (~10 ms)
+    n_d, w_d = 300, 30
+    for m in (16, 128):
+        inp = sharded_inputs(torch, plugins, "decode", m, world, rank)
+        ms = time_sharded(torch, sharded_step(torch, capi, sharded, inp, "rotate", stream_h),
+                          "rotate", n_d, w_d, flush, world)
+        dec[f"m{m}"] = {"us_per_step": ms * 1e3, "n_per_rank": inp["n_loc"], "steps": n_d,
+                        "warmup": w_d, "roofline": sharded_roofline(inp, ms, world, hbm_gbs)}
+        launches += n_d + w_d
+        del inp
+        torch.cuda.empty_cache()
+    out["decode"] = dec
     inp = sharded_inputs(torch, plugins, "prefill", 0, world, rank)
     n_p = max(3, min(steps, 20))
     pre = {"workload": inp["name"], "n_per_rank": inp["n_loc"], "steps": n_p,
@@ -743,20 +763,6 @@ def sharded_summary(torch, plugins, capi, world, rank, steps, warmup, flush, str
     out["prefill"] = pre
     del inp
     torch.cuda.empty_cache()
-    dec = {"workload": "decode_m{16,128}_n28672_k8192", "scaling": "strong",
-           "l2": "weight copies (> 3 x L2 together) in rotation, calls back to back"}
-    # decode calls take ~15-30 us: a fixed 300 back-to-back calls after 30 untimed ones (~10 ms)
-    n_d, w_d = 300, 30
-    for m in (16, 128):
-        inp = sharded_inputs(torch, plugins, "decode", m, world, rank)
-        ms = time_sharded(torch, sharded_step(torch, capi, sharded, inp, "rotate", stream_h),
-                          "rotate", n_d, w_d, flush, world)
-        dec[f"m{m}"] = {"us_per_step": ms * 1e3, "n_per_rank": inp["n_loc"], "steps": n_d,
-                        "warmup": w_d, "roofline": sharded_roofline(inp, ms, world, hbm_gbs)}
-        launches += n_d + w_d
-        del inp
-        torch.cuda.empty_cache()
-    out["decode"] = dec
     return out, launches
 
 

@@ -163,6 +163,10 @@ struct Params {
   // bf16 D of a single destination: base and row pitch in elements (direct-store epilogue)
   uint16_t* d;
   int64_t ldd;
+  // every destination's base (this rank's column slice of each rank's D, local first; row pitch
+  // ldd): the split-K epilogue stores its sums to each
+  uint16_t* dsts[8];
+  int ndst;
 };
 
 // Tile order: the M x N tile grid is walked in bands of kGroupM tile rows, column by column
@@ -284,7 +288,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
   constexpr bool kPair = C::PAIR;
   constexpr int kSplit = C::KSPLIT;
   static_assert(MODE == kEpiBf16 || C::BN == 256, "epilogue variants use 256-column tiles");
-  static_assert(kSplit == 1 || (MODE == kEpiBf16 && NDST == 1), "split K: plain bf16 output");
+  static_assert(kSplit == 1 || MODE == kEpiBf16, "split K: bf16 output");
   constexpr int kGroup = C::CTAS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -640,11 +644,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
               s2 = __fadd_rn(s2, __uint_as_float(part[h][t].z));
               s3 = __fadd_rn(s3, __uint_as_float(part[h][t].w));
             }
-            *reinterpret_cast<uint2*>(p.d + int64_t(m_cta + tk / kQuads) * p.ldd + n0 + col) =
+            const uint2 v =
                 make_uint2(ptx::scaled_f32x2_to_bf16x2(__float_as_uint(s0), __float_as_uint(s1), alpha2),
                            ptx::scaled_f32x2_to_bf16x2(__float_as_uint(s2), __float_as_uint(s3), alpha2));
+            const int64_t off = int64_t(m_cta + tk / kQuads) * p.ldd + n0 + col;
+            // all-gather form: the same 8 bytes into every rank's D, local first, then the peers'
+            // over NVLink (a warp's lanes write consecutive quads of a row)
+#pragma unroll 1
+            for (int i = 0; i < (NDST == 1 ? 1 : p.ndst); ++i)
+              *reinterpret_cast<uint2*>(p.dsts[i] + off) = v;
           }
         }
+        // stores into other GPUs' memory are complete and visible system-wide before the kernel
+        // ends (the caller orders the ranks' reads after every rank's kernel)
+        if constexpr (NDST > 1) __threadfence_system();
       }
     } else {
     int acc = 0;
@@ -1042,6 +1055,10 @@ int launch(const void* A, const void* B, const void* A_sf, const void* B_sf,
   p.sf_pitch = qd.sf_pitch;
   p.d = static_cast<uint16_t*>(dd.base[0]);
   p.ldd = int64_t(dd.row_bytes / 2);
+  static_assert(kMaxRanks <= 8, "Params::dsts");
+  for (int i = 0; i < kMaxRanks; ++i)
+    p.dsts[i] = i < dd.count ? static_cast<uint16_t*>(dd.base[i]) : nullptr;
+  p.ndst = dd.count;
   const int64_t tiles = int64_t(p.m_blocks) * p.n_blocks;
   if (tiles > 0x7FFFFFFF / 16) return NVFP4_ERR_TOO_LARGE;
   // Split K: one cluster of KSPLIT CTAs per tile (clusters beyond what fits at once run as
@@ -1173,11 +1190,20 @@ int run_allgather(const void* A, const void* B, const void* A_sf, const void* B_
   if (!A || !B || !A_sf || !B_sf) return NVFP4_ERR_INVALID_VALUE;
   if (!aligned_to(A, 16) || !aligned_to(B, 16) || !aligned_to(A_sf, 16) || !aligned_to(B_sf, 16))
     return NVFP4_ERR_MISALIGNED;
-  if (M > kRowsPerCta)
-    return launch<CfgPair, kMaxRanks>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N_local, K,
-                                      stream);
-  return launch<CfgSingle, kMaxRanks>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N_local, K,
-                                      stream);
+  // Decode shapes take the split-K forms of the plain GEMM (their epilogue stores each sum into
+  // every rank's D); other shapes the 256-column tiles, whose epilogue TMA-stores each staged box.
+  const int sms = M > kRowsPerCta ? 0 : current_device_sm_count(nullptr);
+#define NVFP4_LAUNCH_AG(CFG) \
+  launch<CFG, kMaxRanks>(A, B, A_sf, B_sf, scale_ptr, scale_val, dd, M, N_local, K, stream)
+  switch (select_plan(M, N_local, K, sms)) {
+    case Plan::kPair: return NVFP4_LAUNCH_AG(CfgPair);
+    case Plan::kSplit4N128: return NVFP4_LAUNCH_AG(CfgSplit4N128);
+    case Plan::kSplit2N128: return NVFP4_LAUNCH_AG(CfgSplit2N128);
+    case Plan::kSplit4: return NVFP4_LAUNCH_AG(CfgSplit4);
+    default: break;
+  }
+  return NVFP4_LAUNCH_AG(CfgSingle);
+#undef NVFP4_LAUNCH_AG
 }
 
 // GEMM with the output quantized to NVFP4 in the epilogue: the bytes of

@@ -198,11 +198,38 @@ def test_gemm_allgather_on_one_gpu_matches_gemm(M, N, K):
             assert np.array_equal(got, full), f"world {world}: output of rank {i} differs"
 
 
+@pytest.mark.parametrize("M,world", [(16, 8), (100, 4), (24, 4), (128, 8)])
+def test_gemm_allgather_split_decode_on_one_gpu(M, world):
+    """Decode shards of a 28672-column weight (K = 2048) with the all-gather fused: each shard
+    takes a split-K form (world 8: 128-column tiles over 4 CTAs; world 4: 128-column tiles over
+    2 above 32 rows, 256-column tiles over 4 at <= 32), whose epilogue stores every sum into each
+    rank's output, here all buffers on this GPU. Every output equals the plain GEMM."""
+    N, K = 28672, 2048
+    rng = np.random.default_rng(M + world)
+    A, B, Asf, Bsf = random_operands(rng, M, N, K)
+    full = capi_gemm(A, B, Asf, Bsf, 0.5)
+    a, asf = to_dev(A, Asf)
+    s = torch.tensor(0.5, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    n_loc = N // world
+    assert capi.gemm_plan(M, n_loc, K)[2] > 1  # the shard does split K
+    outs = [torch.full((M, N), -1, dtype=torch.int16, device="cuda") for _ in range(world)]
+    for r in range(world):
+        b, bsf = to_dev(B[r * n_loc:(r + 1) * n_loc], Bsf[r * n_loc:(r + 1) * n_loc])
+        capi.check(capi.gemm_allgather(a.data_ptr(), b.data_ptr(), asf.data_ptr(), bsf.data_ptr(),
+                                       s.data_ptr(), [o.data_ptr() for o in outs], r, M, n_loc, K,
+                                       stream), "nvfp4_gemm_allgather")
+    torch.cuda.synchronize()
+    for i, o in enumerate(outs):
+        assert np.array_equal(o.cpu().numpy().view(np.uint16), full), f"output of rank {i} differs"
+
+
 @pytest.mark.parametrize("M", [16, 128])
 def test_gemm_narrow_tiles_of_sharded_decode_bit_identical(plugins, M):
     """A decode-shape weight split into 2, 4 or 8 column shards leaves too few 256-column tiles
-    per shard, so the shards run with 128-, 64- and 32-column tiles; every output element is
-    still the same MMA chain over K, so the shards reproduce the unsharded product bit for bit."""
+    per shard: the 2-way shards run 128-column tiles, the 4- and 8-way shards split K over a
+    cluster (fp32 partials summed in a fixed order). The shards reproduce the unsharded product
+    bit for bit."""
     rng = np.random.default_rng(M + 11)
     N, K = 28672, 2048
     A, B, Asf, Bsf = random_operands(rng, M, N, K)

@@ -32,10 +32,12 @@ def test_two_rank_sharded_quantize_gemm_gather():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("M,n_loc,K", [(300, 520, 2560), (96, 1024, 512)])
+@pytest.mark.parametrize("M,n_loc,K", [(300, 520, 2560), (96, 1024, 512), (16, 3584, 2048),
+                                       (100, 7168, 2048)])
 def test_fused_allgather_two_gpus_one_process(M, n_loc, K):
     """The fused GEMM + all-gather with both ranks driven from one process (peer access instead of
-    IPC handles): every rank's output equals the single-GPU GEMM bit for bit."""
+    IPC handles): every rank's output equals the single-GPU GEMM bit for bit. The decode shards
+    (16 x 3584, 100 x 7168) take split-K forms, whose epilogue stores each sum to both GPUs."""
     cmd = ["timeout", "-k", "30", "300", sys.executable, os.path.join(HERE, "fused_allgather_1proc.py"),
            "2", str(M), str(n_loc), str(K), "2"]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=360)
