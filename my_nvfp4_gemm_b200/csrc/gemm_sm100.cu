@@ -669,13 +669,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CU
       const int n0 = nb * C::BN;
       const bool ok = ptx::mbar_wait<kPair>(&tfull_bar[acc], acc_phase, abort_flag, p.timeout_ns);
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
-      // Direct-store form (at most 32 rows): once the CTA's last accumulator is complete its loads
-      // and MMAs are over and its epilogue is short, so the next kernel on the stream may launch
-      // now (onto SMs as they free up); it still waits for this grid's completion before reading
-      // memory. Measured on decode shapes: 1.2-1.6 us per call for M = 16 and 32; with the
-      // longer, TMA-store epilogue of more rows the early launch was slower.
+      // Single-CTA bf16 form: once the CTA's last accumulator is complete its loads and MMAs are
+      // over, so the next kernel on the stream may launch now (onto SMs as they free up); it
+      // still waits for this grid's completion before reading memory. Measured on decode
+      // shapes, per call: 1.2-1.6 us for M = 16 and 32 (direct stores), 0.1-1.1 us for
+      // M = 64 and 128 (ring-staged TMA stores).
       if constexpr (kRingStage)
-        if (p.m <= 32 && ew == 0 && lane == 0 && tile + tile_step >= num_tiles)
+        if (ew == 0 && lane == 0 && tile + tile_step >= num_tiles)
           ptx::griddep_launch_dependents();
       ptx::tc_fence_after_sync();
       const uint32_t t_row = tmem_base + (uint32_t(ew * 32) << 16) + uint32_t(acc * C::BN);
