@@ -284,6 +284,30 @@ def time_device_streaming(torch, fn, steps, warmup, world):
     return max_over_ranks(torch, world, s.elapsed_time(e))
 
 
+def time_graph_streaming(torch, fn, calls, replays, world):
+    """`calls` launches of fn(stream) captured once into a CUDA graph, replayed `replays` times
+    between one pair of CUDA events after one untimed replay: the device time per launch without
+    the host's launch overhead (ms, max over ranks)."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        h = torch.cuda.current_stream().cuda_stream
+        for _ in range(calls):
+            fn(h)
+    g.replay()
+    stream = torch.cuda.current_stream()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    s.record(stream)
+    for _ in range(replays):
+        g.replay()
+    e.record(stream)
+    torch.cuda.synchronize()
+    barrier(torch, world)
+    del g
+    return max_over_ranks(torch, world, s.elapsed_time(e)) / (calls * replays)
+
+
 def cpu_gemm_timer(qa, fa, qb, fb, scale):
     """One step of the reference arithmetic on the host (the oracle port): decode both
     block-scaled operands (oracle, OpenMP), fp32 matmul (torch, all host threads), / scale,
@@ -687,11 +711,12 @@ def sharded_step(torch, capi, sharded, inp, mode, stream_h):
         inp["n_copies"] = n_copies
     turn = [0]
 
-    def step():
+    def step(stream=None):
         wc, wc_sf = weights[turn[0]]
         turn[0] = (turn[0] + 1) % len(weights)
         capi.check(capi.gemm(x.data_ptr(), wc.data_ptr(), x_sf.data_ptr(), wc_sf.data_ptr(),
-                             scale.data_ptr(), d.data_ptr(), M, n_loc, K, stream_h), "nvfp4_gemm")
+                             scale.data_ptr(), d.data_ptr(), M, n_loc, K,
+                             stream_h if stream is None else stream), "nvfp4_gemm")
     return step
 
 
@@ -736,11 +761,15 @@ def sharded_summary(torch, plugins, capi, world, rank, steps, warmup, flush, str
     n_d, w_d = 300, 30
     for m in (16, 128):
         inp = sharded_inputs(torch, plugins, "decode", m, world, rank)
-        ms = time_sharded(torch, sharded_step(torch, capi, sharded, inp, "rotate", stream_h),
-                          "rotate", n_d, w_d, flush, world)
+        step = sharded_step(torch, capi, sharded, inp, "rotate", stream_h)
+        ms = time_sharded(torch, step, "rotate", n_d, w_d, flush, world)
+        # the same rotation captured into a CUDA graph (as a serving loop would run a decode step)
+        ms_g = time_graph_streaming(torch, step, 100, 5, world)
         dec[f"m{m}"] = {"us_per_step": ms * 1e3, "n_per_rank": inp["n_loc"], "steps": n_d,
-                        "warmup": w_d, "roofline": sharded_roofline(inp, ms, world, hbm_gbs)}
-        launches += n_d + w_d
+                        "warmup": w_d, "roofline": sharded_roofline(inp, ms, world, hbm_gbs),
+                        "graph_us_per_step": ms_g * 1e3,
+                        "graph": "100 calls captured once, 5 replays timed after 1"}
+        launches += n_d + w_d + 100 * 6
         del inp
         torch.cuda.empty_cache()
     out["decode"] = dec
@@ -833,6 +862,11 @@ def run_sharded_workload(args):
         "gpu_launches": args.steps * (4 if mode == "nccl" else 1),
         "clocks": sampler.summary(),
     }
+    if mode == "rotate":
+        # the same rotation captured into a CUDA graph: the per-call device time without the
+        # host's launch overhead
+        line["graph_us_per_step"] = time_graph_streaming(torch, step, 100, 5, world) * 1e3
+        line["gpu_launches"] += 100 * 6
     if swiglu and world == 1:
         # the unfused equivalent: bf16 D of the gate+up GEMM, then torch silu(g) * u
         import torch.nn.functional as F
