@@ -60,8 +60,9 @@ def main():
         fused = sharded.gemm_column_parallel(x, w_sh, x_sf, w_sf_sh, sX * sW, gather=True,
                                              fused=True)
         assert torch.equal(fused.view(torch.int16), full.view(torch.int16)), f"fused D differs ({it})"
-    # decode-sized M (single-CTA form of the kernel) and a ragged M
-    for m in (96, 300):
+    # decode-sized M (on this 1024-column shard: K split over clusters of 4 CTAs, whose epilogue
+    # stores every sum into both ranks' outputs) and a ragged M (the CTA-pair form)
+    for m in (16, 96, 300):
         fm = sharded.gemm_column_parallel(x[:m].contiguous(), w_sh, x_sf[:m].contiguous(), w_sf_sh,
                                           sX * sW, gather=True, fused=True)
         assert torch.equal(fm.view(torch.int16), full[:m].view(torch.int16)), f"fused D differs (M={m})"
